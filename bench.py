@@ -1,0 +1,367 @@
+"""Benchmark: RecoverSSM verify + commit seq-steps/sec on B200.
+
+One step = one speculative verify over a batch (gdn_recoverssm_verify) plus the
+commit of the accepted prefixes (GDNRecoverSSMCommitContext.commit: plan +
+fold, conv compaction excluded as in the byte model) on one GDN layer of the
+named configuration (default: config 2, B=512, H=16, HV=32, K=V=128, Q=4,
+prefix-cache align mode with 64-token blocks, bf16 q/k/v, fp32 state pool of
+4096 pages, packed fp32 records).  Synthetic, seeded inputs of those shapes.
+
+Multi-GPU (torchrun, one process per GPU): value heads (and their key heads)
+are sharded across ranks, each rank owning the state pool of its heads; the
+launches are independent, with no collective in the path (host barrier and a
+MAX reduction of the timings only, outside the timed region).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl b200|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gdn-recoverssm-ascend_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "verify+commit seq-steps/sec"
+UNIT = "seq-steps/s"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_profile(cfg):
+    """Per-launch DRAM traffic of the fold kernel from the committed ncu
+    summary (scaled to this workload's units), or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    entry = d.get(f"fold_config{cfg}")
+    return entry
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_baseline(cfg, *, rows_sample, seed=0, repeats=1):
+    """Time the oracle's torch CPU executors (all host threads) on a bounded
+    sample of the workload: `rows_sample` sequence rows with every head."""
+    from gdn_recoverssm_b200 import synthetic
+    from oracle import cpu_executors as X
+
+    spec = dict(synthetic.CONFIGS[cfg])
+    B, H, HV, D, Q = rows_sample, spec["H"], spec["HV"], spec["D"], spec["Q"]
+    gen = torch.Generator().manual_seed(seed)
+    T = B * Q
+    act = spec["act"]
+    unit = lambda x: x / x.norm(dim=-1, keepdim=True)  # noqa: E731
+    q = unit(torch.randn(T, H, D, generator=gen)).to(act)
+    k = unit(torch.randn(T, H, D, generator=gen)).to(act)
+    v = torch.randn(T, HV, D, generator=gen).to(act)
+    g = -torch.nn.functional.softplus(torch.randn(T, HV, generator=gen))
+    beta = torch.sigmoid(torch.randn(T, HV, generator=gen))
+    pool = 2 * B + 1
+    state = torch.randn(pool, HV, D, D, generator=gen) * 0.1
+    src = torch.arange(1, B + 1, dtype=torch.int32)
+    fin = torch.arange(B + 1, 2 * B + 1, dtype=torch.int32)
+    qsl = torch.arange(B + 1, dtype=torch.int32) * Q
+    acc = torch.randint(1, Q + 1, (B,), generator=gen, dtype=torch.int32)
+    records = torch.zeros(B, HV, Q, 2 * D + 1)
+    out = torch.zeros(T, HV, D, dtype=act)
+    zeros = torch.zeros(B, dtype=torch.int32)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        X.verify_packed(q, k, v, g, beta, state, qsl, src, records, out, spec_query_len=Q, scale=D**-0.5)
+        X.fold_packed(state, records, src, acc, fin, zeros, zeros, rows=B)
+        times.append(time.perf_counter() - t0)
+    t = min(times)
+    return {"value": B / t, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"config {cfg}: {B} of {spec['B']} rows x {HV} value heads, verify + fold, best of {repeats}",
+            "seconds_per_sample": t}
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return 0
+    from gdn_recoverssm_b200 import synthetic
+
+    spec = synthetic.CONFIGS[args.config]
+    rows = args.cpu_rows
+    for _ in range(max(args.warmup, 0) and 1):
+        cpu_baseline(args.config, rows_sample=max(1, rows // 8))
+    vals = []
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(args.config, rows_sample=rows)["value"])
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * spec["B"] / value, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": _config_dict(args.config, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"each step: {rows} of {spec['B']} rows x all heads (verify + fold), torch CPU "
+                                   f"executors restating the reference's CPU path"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def _config_dict(cfg, world):
+    from gdn_recoverssm_b200 import synthetic
+
+    s = synthetic.CONFIGS[cfg]
+    mode = "align (block %d)" % s["block"] if s["align"] else "none"
+    return {
+        "workload": f"config{cfg}: B={s['B']} H={s['H']} HV={s['HV']} K=V={s['D']} Q={s['Q']} {mode}, "
+                    f"{str(s['act']).split('.')[-1]} q/k/v, fp32 state pool {s['pool']} pages, packed fp32 records",
+        "global_batch": s["B"],
+        "spec_query_len": s["Q"],
+        "parallelism": f"v-head shards x{world} (no collective)",
+        "l2": "inputs larger than L2: every step reads all B x HV state tiles (64 KiB each)",
+    }
+
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    import gdn_recoverssm_b200 as g
+    from gdn_recoverssm_b200 import _native, synthetic
+
+    _native.ops()
+    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=16)
+    stream = torch.cuda.current_stream(dev)
+    ctx = g.GDNRecoverSSMCommitContext.from_tensors([wl.conv], [wl.state], [wl.records], spec_query_len=wl.Q,
+                                                    max_num_reqs=wl.B)
+    align_kw = {}
+    if wl.block_table is not None:
+        align_kw = dict(block_table=wl.block_table, num_computed_tokens=wl.num_computed,
+                        mamba_block_size=wl.block_size)
+
+    def verify():
+        g.gdn_recoverssm_verify(wl.g, wl.beta, wl.q, wl.k, wl.v, checkpoint_state=wl.state, replay_cache=wl.records,
+                                query_start_loc=wl.qsl, state_indices=wl.state_indices, spec_query_len=wl.Q,
+                                out=wl.out)
+
+    specs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=False, **align_kw)
+    plan_spec, fold_spec = specs[0], specs[-1]
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        verify()
+        plan_spec.launch()
+        fold_spec.launch()
+    barrier()
+    # plan outputs are identical every step (same metadata): byte model inputs
+    lens = ctx.commit_lens[: wl.B].cpu()
+    bnd = ((ctx.boundary_state_indices[: wl.B] > 0) & (ctx.boundary_recovery_lens[: wl.B] > 0)
+           & (ctx.boundary_state_indices[: wl.B] != ctx.final_state_indices[: wl.B])).cpu()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        barrier()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            e = ev[i]
+            e[0].record(stream)
+            verify()
+            e[1].record(stream)
+            plan_spec.launch()
+            e[2].record(stream)
+            fold_spec.launch()
+            e[3].record(stream)
+        t_end.record(stream)
+        barrier()
+        # end to end through the public API with host buffers
+        e2e = _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier)
+    total_ms = t_start.elapsed_time(t_end)
+    verify_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    plan_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    fold_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
+    step_ms = total_ms / args.steps
+    t = torch.tensor([step_ms, verify_ms, plan_ms, fold_ms, e2e["ms"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, verify_ms, plan_ms, fold_ms, e2e_ms = t.tolist()
+    clk = clocks.summary()
+    status = int(torch.ops.gdn_recoverssm_ac.device_status())
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = _peaks()
+    vbytes = synthetic.verify_bytes(wl)
+    fbytes = synthetic.commit_bytes(wl, lens, int(bnd.sum()))
+    fold_gbs = fbytes / (fold_ms * 1e-3) / 1e9
+    verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
+    step_gbs = (vbytes + fbytes) / (step_ms * 1e-3) / 1e9
+    traffic = _traffic_profile(args.config)
+    value = wl.B / (step_ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": _config_dict(args.config, world),
+        "e2e": {"value": wl.B / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"],
+                "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms},
+        "roofline": {"bound": "hbm", "kernel": "fold (grouped commit)", "achieved": fold_gbs, "peak": peak,
+                     "unit": "GB/s", "frac": fold_gbs / peak, "peak_kind": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": fbytes},
+        "kernels": {
+            "verify": {"ms": verify_ms, "bytes": vbytes, "GB/s": verify_gbs, "frac": verify_gbs / peak},
+            "commit_plan": {"ms": plan_ms},
+            "fold": {"ms": fold_ms, "bytes": fbytes, "GB/s": fold_gbs, "frac": fold_gbs / peak},
+            "step": {"GB/s": step_gbs, "frac": step_gbs / peak, "per_rank_bytes": vbytes + fbytes},
+        },
+        "gpu_launches": 3 * args.steps,
+        "clocks": clk,
+        "device_status": status,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(args.config, rows_sample=args.cpu_rows)
+    print(json.dumps(line))
+    return 0
+
+
+def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier):
+    """Same step through the public API from pinned host buffers: H2D of the
+    step's inputs (q, k, v, g, beta and the row metadata), verify + commit,
+    D2H of the attention output."""
+    host = {n: getattr(wl, n).cpu().pin_memory() for n in ("q", "k", "v", "g", "beta", "qsl", "state_indices",
+                                                          "accepted")}
+    if align_kw:
+        host["block_table"] = wl.block_table.cpu().pin_memory()
+        host["num_computed"] = wl.num_computed.cpu().pin_memory()
+    dev_in = {n: torch.empty_like(t, device=dev) for n, t in host.items()}
+    out_host = torch.empty(wl.out.shape, dtype=wl.out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+    steps = max(1, args.steps // 4)
+
+    def step():
+        for n, t in host.items():
+            dev_in[n].copy_(t, non_blocking=True)
+        kw = {}
+        if align_kw:
+            kw = dict(block_table=dev_in["block_table"], num_computed_tokens=dev_in["num_computed"],
+                      mamba_block_size=wl.block_size)
+        g.gdn_recoverssm_verify(dev_in["g"], dev_in["beta"], dev_in["q"], dev_in["k"], dev_in["v"],
+                                checkpoint_state=wl.state, replay_cache=wl.records, query_start_loc=dev_in["qsl"],
+                                state_indices=dev_in["state_indices"], spec_query_len=wl.Q, out=wl.out)
+        ctx.commit(dev_in["accepted"], dev_in["state_indices"], dev_in["qsl"], commit_conv=False, **kw)
+        out_host.copy_(wl.out, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    barrier()
+    return {"ms": a.elapsed_time(b) / steps, "h2d": h2d, "d2h": d2h}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description="RecoverSSM verify+commit benchmark")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=16, help="rows in the CPU baseline's bounded sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,85 @@
+// Fold / plan / conv-compaction launchers.
+#include "fold.cuh"
+#include "plan.cuh"
+
+GDN_RSSM_STATUS_WORD(fold)
+
+namespace gdn_rssm {
+
+template <int DIM, typename St, typename Kt>
+int launch_fold_variant(FoldParams p, cudaStream_t stream) {
+  p.status = status_ptr_for_device<symbol_fold>();
+  if (p.status == nullptr) {
+    set_error("GDN RecoverSSM: cannot resolve the device status word");
+    return GDN_RSSM_ECUDA;
+  }
+  const int64_t grid = p.layers * p.rows * p.heads;
+  fold_kernel<DIM, St, Kt><<<static_cast<unsigned>(grid), kFoldThreads, 0, stream>>>(p);
+  GDN_CUDA(cudaGetLastError());
+  return GDN_RSSM_OK;
+}
+
+template <int DIM, typename St>
+int launch_fold_key(const FoldParams &p, int32_t key_dtype, cudaStream_t stream) {
+  switch (key_dtype) {
+    case GDN_RSSM_F32: return launch_fold_variant<DIM, St, float>(p, stream);
+    case GDN_RSSM_BF16: return launch_fold_variant<DIM, St, __nv_bfloat16>(p, stream);
+    case GDN_RSSM_F16: return launch_fold_variant<DIM, St, __half>(p, stream);
+  }
+  set_error("GDN RecoverSSM: unsupported record key dtype");
+  return GDN_RSSM_EUNSUPPORTED;
+}
+
+template <typename St>
+int launch_fold_dim(const FoldParams &p, int dim, int32_t key_dtype, cudaStream_t stream) {
+  switch (dim) {
+    case 32: return launch_fold_key<32, St>(p, key_dtype, stream);
+    case 64: return launch_fold_key<64, St>(p, key_dtype, stream);
+    case 128: return launch_fold_key<128, St>(p, key_dtype, stream);
+  }
+  set_error("GDN RecoverSSM: unsupported fold head dim");
+  return GDN_RSSM_EUNSUPPORTED;
+}
+
+int launch_fold(const FoldParams &p, int dim, int32_t state_dtype, int32_t key_dtype, cudaStream_t stream) {
+  if (state_dtype == GDN_RSSM_F32) return launch_fold_dim<float>(p, dim, key_dtype, stream);
+  if (state_dtype == GDN_RSSM_BF16) return launch_fold_dim<__nv_bfloat16>(p, dim, key_dtype, stream);
+  set_error("GDN RecoverSSM: fold state must be FP32 or BF16");
+  return GDN_RSSM_EUNSUPPORTED;
+}
+
+static unsigned blocks_for(int64_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
+
+int launch_commit_plan(const CommitPlanParams &p, cudaStream_t stream) {
+  commit_plan_kernel<<<blocks_for(p.rows, 128), 128, 0, stream>>>(p);
+  GDN_CUDA(cudaGetLastError());
+  return GDN_RSSM_OK;
+}
+
+int launch_grouped_plan(const GroupedPlanParams &p, cudaStream_t stream) {
+  grouped_plan_kernel<<<blocks_for(p.rows, 128), 128, 0, stream>>>(p);
+  GDN_CUDA(cudaGetLastError());
+  return GDN_RSSM_OK;
+}
+
+int launch_publish_align(const PublishParams &p, cudaStream_t stream) {
+  publish_align_kernel<<<blocks_for(p.rows, 128), 128, 0, stream>>>(p);
+  GDN_CUDA(cudaGetLastError());
+  return GDN_RSSM_OK;
+}
+
+int launch_compact_conv(const ConvParams &p, int elem_size, cudaStream_t stream) {
+  const int64_t grid = p.layers * p.rows;
+  const int threads = 256;
+  switch (elem_size) {
+    case 2: compact_conv_kernel<uint16_t><<<static_cast<unsigned>(grid), threads, 0, stream>>>(p); break;
+    case 4: compact_conv_kernel<uint32_t><<<static_cast<unsigned>(grid), threads, 0, stream>>>(p); break;
+    default:
+      set_error("GDN RecoverSSM: conv state element size must be 2 or 4 bytes");
+      return GDN_RSSM_EUNSUPPORTED;
+  }
+  GDN_CUDA(cudaGetLastError());
+  return GDN_RSSM_OK;
+}
+
+}  // namespace gdn_rssm

@@ -1,0 +1,203 @@
+// Commit-plan, align-publication and conv-compaction kernels (integer /
+// byte work, bit-exact with the reference).
+//
+//  * commit_plan_kernel  <- _prepare_commit_plan_kernel (kernels.py:936-1072)
+//  * grouped_plan_kernel <- _grouped_plan_kernel (grouped_commit.py:31-222)
+//  * publish_align_kernel <- _publish_grouped_align_kernel (grouped_commit.py:531-560)
+//  * compact_conv_kernel <- _grouped_compact_conv_state_kernel
+//    (grouped_commit.py:225-322) / _compact_conv_state_kernel
+//    (kernels.py:1075-1169)
+//
+// One thread per plan row (the reference launches one single-warp program per
+// row).  Every table read is bounds-checked against the lengths the host
+// passes: a row whose request index falls outside `sampled`, the block table
+// or `num_computed` becomes an invalid (no-op) row instead of an out-of-bounds
+// read.
+#pragma once
+
+#include "params.cuh"
+
+namespace gdn_rssm {
+
+
+__global__ void commit_plan_kernel(const CommitPlanParams p) {
+  const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (r >= p.rows) return;
+  const int64_t nul = p.null_block;
+  const int64_t source = load_index(p.state, r);
+  const int64_t req = p.request.data ? load_index(p.request, r) : r;
+  bool row_ok = true;
+  const int64_t acc = load_index_checked(p.accepted, req, row_ok);
+  const int64_t bos = load_index(p.qsl, r), eos = load_index(p.qsl, r + 1);
+  const int32_t qlen = static_cast<int32_t>(eos - bos);
+  int64_t n = acc > 0 ? acc : 0;
+  n = n < qlen ? n : qlen;
+  n = n < p.Q ? n : p.Q;
+  int64_t fin = source, boundary = nul, blen = 0, colv = 0, c = 0;
+  const bool align = p.table.data != nullptr;
+  if (align) {
+    c = static_cast<int32_t>(load_index_checked(p.computed, req, row_ok));
+    if (req < 0 || req >= p.table.rows) row_ok = false;
+    const int64_t W = p.table.cols, B = p.block_size;
+    const int64_t end = c + n;
+    colv = floordiv(end - 1 > 0 ? end - 1 : 0, B);
+    colv = colv < W - 1 ? colv : W - 1;
+    fin = row_ok ? load_table(p.table, req, colv) : nul;
+    const int64_t nxt = (floordiv(c, B) + 1) * B;
+    const bool crosses = end >= nxt;
+    blen = nxt - c;
+    const int64_t bcol = floordiv(nxt, B) - 1;
+    boundary = (row_ok && crosses && bcol >= 0 && bcol < W) ? load_table(p.table, req, bcol) : nul;
+  }
+  const bool geometry = bos >= 0 && bos <= eos && qlen <= p.Q;
+  bool valid = row_ok && source > nul && source < p.num_blocks && fin > nul && fin < p.num_blocks && geometry && n > 0 &&
+               n <= qlen;
+  if (align) {
+    valid = valid && c >= 0;
+    if (!(boundary > nul && boundary < p.num_blocks)) blen = 0;
+  }
+  p.lens[r] = valid ? static_cast<int32_t>(n) : 0;
+  p.finals[r] = static_cast<int32_t>(valid ? fin : nul);
+  p.boundaries[r] = static_cast<int32_t>(valid ? boundary : nul);
+  p.boundary_lens[r] = valid ? static_cast<int32_t>(blen) : 0;
+  p.valid[r] = valid ? 1 : 0;
+  p.col[r] = static_cast<int32_t>(colv);
+}
+
+
+__global__ void grouped_plan_kernel(const GroupedPlanParams p) {
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (row >= p.rows) return;
+  const int64_t nul = p.null_block;
+  bool all_valid = true;
+  int64_t shared_col = -1, shared_req = -1;
+  for (int gi = 0; gi < p.num_groups; ++gi) {
+    const gdn_rssm_plan_group &g = p.groups[gi];
+    const int64_t req = load_index(g.request_indices, row);
+    const int64_t source = load_index(g.state_indices, row);
+    const int64_t bos = load_index(g.query_start_loc, row), eos = load_index(g.query_start_loc, row + 1);
+    const int64_t qlen = eos - bos;
+    bool row_ok = true;
+    const int64_t acc = static_cast<int32_t>(load_index_checked(p.sampled, req, row_ok));
+    int64_t n = acc > 0 ? acc : 0;
+    n = n < qlen ? n : qlen;
+    n = n < p.Q ? n : p.Q;
+    int64_t fin = source, boundary = nul, blen = 0, colv = 0;
+    bool computed_ok = true;
+    if (p.align) {
+      const int64_t c = load_index_checked(g.num_computed, req, row_ok);
+      if (req < 0 || req >= g.block_table.rows) row_ok = false;
+      computed_ok = c >= 0;
+      const int64_t B = g.block_size, W = g.block_table.cols;
+      const int64_t pos = c + n;
+      colv = floordiv(pos - 1 > 0 ? pos - 1 : 0, B);
+      colv = colv < W - 1 ? colv : W - 1;
+      fin = row_ok ? load_table(g.block_table, req, colv) : nul;
+      const int64_t nxt = (floordiv(c, B) + 1) * B;
+      const bool crossed = pos >= nxt;
+      blen = static_cast<int32_t>(nxt - c);
+      const int64_t bcol = floordiv(nxt, B) - 1;
+      boundary = (row_ok && crossed && computed_ok && bcol >= 0 && bcol < W) ? load_table(g.block_table, req, bcol) : nul;
+    }
+    const bool geometry = bos >= 0 && bos <= eos && qlen <= p.Q;
+    bool valid = row_ok && geometry && source > nul && source < g.num_blocks && fin > nul && fin < g.num_blocks &&
+                 n > 0 && n <= qlen && computed_ok;
+    if (!(boundary > nul && boundary < g.num_blocks)) {
+      blen = 0;
+      boundary = nul;
+    }
+    const int64_t off = gi * p.capacity + row;
+    p.source[off] = static_cast<int32_t>(valid ? source : nul);
+    p.length[off] = valid ? static_cast<int32_t>(n) : 0;
+    p.finals[off] = static_cast<int32_t>(valid ? fin : nul);
+    p.boundaries[off] = static_cast<int32_t>(valid ? boundary : nul);
+    p.boundary_lens[off] = valid ? static_cast<int32_t>(blen) : 0;
+    p.valid[off] = valid ? 1 : 0;
+    p.col[off] = static_cast<int32_t>(colv);
+    if (gi == 0) {
+      shared_col = colv;
+      shared_req = req;
+    } else {
+      all_valid = all_valid && colv == shared_col && req == shared_req;
+    }
+    all_valid = all_valid && valid;
+  }
+  if (p.align && p.publish) {
+    bool ok = true;
+    const int64_t slot = load_index_checked(p.idx_mapping, shared_req, ok, -1);
+    if (all_valid && ok && slot >= 0 && slot < p.cols_out.length && slot < p.accepted_out.length) {
+      store_index(p.cols_out, slot, shared_col);
+      store_index(p.accepted_out, slot, 1);
+    }
+  }
+}
+
+
+__global__ void publish_align_kernel(const PublishParams p) {
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (row >= p.rows) return;
+  const int32_t *first_cols = reinterpret_cast<const int32_t *>(p.descriptors[1]);
+  const int32_t shared = first_cols[row];
+  bool ok = true;
+  for (int b = 0; b < p.num_buckets; ++b) {
+    const int64_t *d = p.descriptors + 4 * b;
+    const int32_t *valid = reinterpret_cast<const int32_t *>(d[0]);
+    const int32_t *col = reinterpret_cast<const int32_t *>(d[1]);
+    const int64_t cap = d[2];
+    const int64_t groups = d[3];
+    for (int64_t gi = 0; gi < groups; ++gi) {
+      const int64_t off = gi * cap + row;
+      ok = ok && valid[off] != 0 && col[off] == shared;
+    }
+  }
+  const int64_t req = load_index(p.request, row);
+  bool in_range = true;
+  const int64_t slot = load_index_checked(p.idx_mapping, req, in_range, -1);
+  if (ok && in_range && slot >= 0 && slot < p.cols_out.length && slot < p.accepted_out.length) {
+    store_index(p.cols_out, slot, shared);
+    store_index(p.accepted_out, slot, 1);
+  }
+}
+
+
+// One CTA per (layer, row); threads stride over the [conv_dim, history] window.
+// Both windows are read into registers before either is stored (the final or
+// the boundary page may alias the source page).
+template <typename E>
+__global__ void compact_conv_kernel(const ConvParams p) {
+  const int64_t row = blockIdx.x % p.rows;
+  const int64_t layer = blockIdx.x / p.rows;
+  const int64_t prow = static_cast<int64_t>(p.layer_groups[layer]) * p.capacity + row;
+  if (prow < 0 || prow >= p.plan_len) return;
+  bool ok = true;
+  const int64_t src = load_index_checked(p.source, prow, ok);
+  const int32_t n = p.lengths[prow];
+  const int64_t fin = p.finals[prow];
+  // n < 1 or a window reaching past the conv state would read outside the
+  // page: such a row is skipped (the plan never produces one).
+  if (!ok || src <= p.null_block || src >= p.num_blocks || n < 1 || n - 1 + p.history > p.window ||
+      fin <= p.null_block || fin >= p.num_blocks)
+    return;
+  const int64_t bidx = p.boundaries[prow];
+  const int32_t blen = p.boundary_lens[prow];
+  const bool do_b = p.align && bidx > p.null_block && bidx < p.num_blocks && blen >= 1 && blen - 1 + p.history <= p.window;
+  E *base = reinterpret_cast<E *>(p.addrs[layer]);
+  const int64_t bs = p.block_strides[layer], ds = p.dim_strides[layer], ts = p.token_strides[layer];
+  const E *srcp = base + src * bs;
+  const int64_t total = p.conv_dim * p.history;
+  // The kernel's own footprint is bounded by what one CTA holds per pass.
+  for (int64_t i0 = 0; i0 < total; i0 += blockDim.x) {
+    const int64_t i = i0 + threadIdx.x;
+    const bool live = i < total;
+    const int64_t d = live ? i / p.history : 0, hh = live ? i % p.history : 0;
+    E fv{}, bv{};
+    if (live) fv = srcp[d * ds + (n - 1 + hh) * ts];
+    if (live && do_b) bv = srcp[d * ds + (blen - 1 + hh) * ts];
+    __syncthreads();  // every read of this pass precedes every store of it
+    if (live && do_b) base[bidx * bs + d * ds + hh * ts] = bv;
+    if (live) base[fin * bs + d * ds + hh * ts] = fv;
+    __syncthreads();
+  }
+}
+
+}  // namespace gdn_rssm

@@ -1,0 +1,91 @@
+// Host launcher for the verify kernel, instantiated once per activation dtype
+// (verify_bf16.cu, verify_f16.cu, verify_f32.cu) so the template variants
+// compile in parallel.  Each instantiating translation unit owns one device
+// status word.
+#pragma once
+
+#include "verify.cuh"
+
+namespace gdn_rssm {
+
+// Everything the launcher needs besides the kernel parameters.
+struct VerifyLaunch {
+  VerifyParams p;
+  const void *state;
+  int64_t state_bs, state_hs, state_vs;  // element strides of the pool
+  int32_t state_dtype;
+  int dim;
+  cudaStream_t stream;
+};
+
+// Encodes the 4-D tiled tensor map of the state pool (defined in capi.cu).
+int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, int dim, int64_t value_heads,
+                     int64_t blocks, int64_t state_bs, int64_t state_hs, int64_t state_vs);
+
+template <int DIM, int QT, typename Act, typename St>
+int launch_verify_variant(VerifyLaunch &L) {
+  CUtensorMap map;
+  int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, L.p.value_heads, L.p.blocks, L.state_bs, L.state_hs,
+                            L.state_vs);
+  if (rc != GDN_RSSM_OK) return rc;
+  constexpr int smem = verify_smem_bytes<DIM, QT, St>();
+  static bool configured[64] = {false};
+  int dev = 0;
+  GDN_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_error("GDN RecoverSSM: device ordinal out of range");
+    return GDN_RSSM_EUNSUPPORTED;
+  }
+  if (!configured[dev]) {
+    GDN_CUDA(cudaFuncSetAttribute(verify_kernel<DIM, QT, Act, St>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured[dev] = true;
+  }
+  const int64_t grid = L.p.rows * L.p.value_heads;
+  verify_kernel<DIM, QT, Act, St><<<static_cast<unsigned>(grid), kVerifyThreads, smem, L.stream>>>(map, L.p);
+  GDN_CUDA(cudaGetLastError());
+  return GDN_RSSM_OK;
+}
+
+template <int DIM, typename Act, typename St>
+int launch_verify_qt(VerifyLaunch &L) {
+  const int64_t Q = L.p.query_len;
+  if (Q <= 1) return launch_verify_variant<DIM, 1, Act, St>(L);
+  if (Q <= 2) return launch_verify_variant<DIM, 2, Act, St>(L);
+  if (Q <= 4) return launch_verify_variant<DIM, 4, Act, St>(L);
+  return launch_verify_variant<DIM, 8, Act, St>(L);
+}
+
+template <typename Act>
+int launch_verify_act(VerifyLaunch &L) {
+  if (L.state_dtype == GDN_RSSM_F32) {
+    switch (L.dim) {
+      case 32: return launch_verify_qt<32, Act, float>(L);
+      case 64: return launch_verify_qt<64, Act, float>(L);
+      case 128: return launch_verify_qt<128, Act, float>(L);
+    }
+  } else if (L.state_dtype == GDN_RSSM_BF16) {
+    switch (L.dim) {
+      case 64: return launch_verify_qt<64, Act, __nv_bfloat16>(L);
+      case 128: return launch_verify_qt<128, Act, __nv_bfloat16>(L);
+    }
+  }
+  set_error("GDN RecoverSSM: unsupported verify state dtype / head dim");
+  return GDN_RSSM_EUNSUPPORTED;
+}
+
+}  // namespace gdn_rssm
+
+// Defines, for activation type ACT and suffix NAME, a device status word
+// (GDN_RSSM_STATUS_WORD) and int gdn_rssm::launch_verify_NAME(VerifyLaunch&).
+#define GDN_RSSM_VERIFY_TU(ACT, NAME)                                    \
+  GDN_RSSM_STATUS_WORD(NAME)                                             \
+  namespace gdn_rssm {                                                   \
+  int launch_verify_##NAME(VerifyLaunch &L) {                            \
+    L.p.status = status_ptr_for_device<symbol_##NAME>();                 \
+    if (L.p.status == nullptr) {                                         \
+      set_error("GDN RecoverSSM: cannot resolve the device status word"); \
+      return GDN_RSSM_ECUDA;                                             \
+    }                                                                    \
+    return launch_verify_act<ACT>(L);                                    \
+  }                                                                      \
+  }

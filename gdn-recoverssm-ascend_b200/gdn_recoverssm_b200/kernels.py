@@ -1,0 +1,515 @@
+"""RecoverSSM verify + per-context commit for Gated DeltaNet on B200 (sm_100a).
+
+Drop-in host layer for the reference module
+``plugin/gdn_recoverssm_ascend/kernels.py``: the same public names, call
+signatures, argument checks (``ValueError("GDN RecoverSSM: ...")`` raised
+before any launch) and buffer contracts, with every launch going to the
+hand-written CUDA kernels through ``torch.ops.gdn_recoverssm_ac`` (the C ABI
+in ``include/gdn_recoverssm_b200.h``).  There is no Triton, no dispatch
+between backends and no CPU fallback: CPU tensors are rejected by the ops.
+
+Public entry points (reference line numbers):
+  * ``gdn_recoverssm_verify``                 kernels.py:700-928
+  * ``ReplayRecordBuffers``                   kernels.py:166-247
+  * ``record_nbytes`` / ``record_geometry_bytes`` kernels.py:250-294
+  * ``GDNRecoverSSMCommitContext.from_tensors`` kernels.py:1421-1565
+  * ``GDNRecoverSSMCommitContext.commit`` / ``make_commit_specs``
+                                              kernels.py:1648-1676,1823-2052
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import dataclass, field
+from typing import Any, Callable
+
+import torch
+
+from . import _native
+
+NULL_BLOCK_ID = 0  # page 0 is the null page
+MAX_SPEC_QUERY_LEN = 8  # window bound of every kernel (kernels.py:101)
+SUPPORTED_HEAD_DIMS = (32, 64, 128)
+
+# flags of the extended native ops (include/gdn_recoverssm_b200.h)
+_RECORD_PACKED = 1
+_NORMALIZE_QK = 2
+_FOLD_PACKED = 1
+
+
+def _require(cond: bool, msg: str) -> None:
+    """Argument validation raising ``ValueError`` before any launch, with the
+    reference's message format (kernels.py:143-151)."""
+    if not cond:
+        raise ValueError(f"GDN RecoverSSM: {msg}")
+
+
+def _ptr_table(tensors: Sequence[torch.Tensor], device) -> torch.Tensor:
+    """int64 table of data pointers keeping each uint64 bit pattern (pointers
+    with the top bit set would overflow a plain int64 conversion)."""
+    ptrs = [t.data_ptr() for t in tensors]
+    ptrs = [p if p < (1 << 63) else p - (1 << 64) for p in ptrs]
+    return torch.tensor(ptrs, dtype=torch.int64, device=device)
+
+
+@dataclass
+class _LaunchSpec:
+    """One native launch: the op and its exact arguments.
+
+    ``make_commit_specs`` / ``GroupedCommitBucket.make_specs`` return these
+    without launching, mirroring the reference's spec objects
+    (kernels.py:1327-1348); ``launch()`` runs the op on the current stream.
+    """
+
+    name: str
+    op: Callable
+    args: tuple
+    kwargs: dict = field(default_factory=dict)
+
+    def launch(self) -> None:
+        self.op(*self.args, **self.kwargs)
+
+    def compile_only(self) -> None:
+        """Kernels are compiled ahead of time (sm_100a); only resolve the op."""
+        _native.ops()
+
+
+@dataclass(frozen=True)
+class ReplayRecordBuffers:
+    """Typed (SoA) per-step records: ``correction [rows, HV, Q, V]`` fp32,
+    ``key [rows, H, Q, K]`` (one key per GQA key head; pre-normalised
+    low-precision keys keep their exact input bits) and ``decay [rows, HV, Q]``
+    fp32 (kernels.py:166-247)."""
+
+    correction: torch.Tensor
+    key: torch.Tensor
+    decay: torch.Tensor
+
+    @property
+    def shape(self) -> tuple[int, int, int, int]:
+        rows, heads, window, value_dim = self.correction.shape
+        return (rows, heads, window, value_dim + self.key.shape[-1] + 1)
+
+    @property
+    def dtype(self):
+        return torch.float32
+
+    @property
+    def device(self):
+        return self.correction.device
+
+    @property
+    def num_key_heads(self) -> int:
+        return int(self.key.shape[1])
+
+    @property
+    def key_dtype(self):
+        return self.key.dtype
+
+    @property
+    def record_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.correction, self.key, self.decay))
+
+    @classmethod
+    def allocate(cls, rows, num_value_heads, num_key_heads, window, value_dim, key_dim, *, device,
+                 key_dtype=torch.float32):
+        _require(
+            rows > 0
+            and num_key_heads > 0
+            and 0 < window <= MAX_SPEC_QUERY_LEN
+            and value_dim > 0
+            and key_dim > 0
+            and num_value_heads > 0
+            and num_value_heads % num_key_heads == 0,
+            "record head/row geometry is invalid",
+        )
+        _require(key_dtype in (torch.float16, torch.bfloat16, torch.float32), "record keys require FP16, BF16 or FP32")
+        return cls(
+            torch.zeros((rows, num_value_heads, window, value_dim), dtype=torch.float32, device=device),
+            torch.zeros((rows, num_key_heads, window, key_dim), dtype=key_dtype, device=device),
+            torch.zeros((rows, num_value_heads, window), dtype=torch.float32, device=device),
+        )
+
+
+def record_nbytes(record) -> int:
+    """Bytes held by one layer's records (packed tensor or typed buffers)."""
+    if isinstance(record, ReplayRecordBuffers):
+        return record.record_bytes
+    return record.numel() * record.element_size()
+
+
+def record_geometry_bytes(rows, num_layers, num_value_heads, num_key_heads, window, key_dim, value_dim,
+                          key_dtype=torch.float32) -> int:
+    """Physical bytes of typed records for a model geometry, keys deduplicated
+    per key head and stored in ``key_dtype`` (kernels.py:258-294)."""
+    _require(min(rows, num_layers, num_value_heads, num_key_heads, window, key_dim, value_dim) > 0,
+             "record geometry must be positive")
+    _require(num_value_heads % num_key_heads == 0, "value heads must be a multiple of key heads")
+    _require(key_dtype in (torch.float16, torch.bfloat16, torch.float32), "record keys require FP16, BF16 or FP32")
+    key_bytes = 4 if key_dtype == torch.float32 else 2
+    per_token = num_value_heads * value_dim * 4 + num_key_heads * key_dim * key_bytes + num_value_heads * 4
+    return rows * num_layers * window * per_token
+
+
+# --------------------------------------------------------------------------- #
+# verify
+# --------------------------------------------------------------------------- #
+def gdn_recoverssm_verify(
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    checkpoint_state: torch.Tensor,
+    replay_cache,
+    query_start_loc: torch.Tensor,
+    state_indices: torch.Tensor,
+    spec_query_len: int,
+    scale: float | None = None,
+    qk_already_normalized: bool = True,
+    out: torch.Tensor | None = None,
+    _collect: list | None = None,
+) -> torch.Tensor:
+    """Verify a speculative window against its checkpoint without modifying the
+    checkpoint (reference kernels.py:700-928).
+
+    ``g`` (log-space decay) and ``beta`` (already sigmoid) are ``[1, T, HV]``
+    or ``[T, HV]``; q, k ``[1, T, H, K]``; v ``[1, T, HV, V]``;
+    ``checkpoint_state`` ``[blocks, HV, V, K]`` (read-only); ``replay_cache``
+    is either a packed fp32 ``[rows, HV, Q, V + K + 1]`` tensor or a
+    ``ReplayRecordBuffers``.  ``qk_already_normalized=False`` L2-normalises
+    q/k inside the kernel (``x * rsqrt(sum(x^2) + 1e-6)``).  Returns ``out``
+    ``[1, T, HV, V]``.  Launches on the current CUDA stream.
+    """
+    _require(q.ndim == 4 and q.shape[0] == 1, "q must have shape [1, tokens, heads, dim]")
+    _, total, H, K = q.shape
+    _require(k.shape == q.shape, "q and k shapes differ")
+    _require(v.ndim == 4 and tuple(v.shape[:2]) == (1, total), "v must have shape [1, tokens, value heads, dim]")
+    HV, V = v.shape[-2], v.shape[-1]
+    _require(H > 0 and HV >= H and HV % H == 0, "value heads must be a positive multiple of the q/k heads")
+    _require(g.numel() == total * HV and beta.numel() == total * HV, "gate or beta shape is incompatible")
+    g2 = g.reshape(total, HV)
+    beta2 = beta.reshape(total, HV)
+    _require(g2.stride(1) == 1 and beta2.stride(1) == 1, "gate and beta heads must be contiguous")
+    _require(0 < spec_query_len <= MAX_SPEC_QUERY_LEN, f"spec_query_len must be in [1, {MAX_SPEC_QUERY_LEN}]")
+    _require(all(t_.stride(-1) == 1 and t_.stride(-2) == K for t_ in (q, k)), "q and k heads must be contiguous")
+    _require(v.stride(-1) == 1 and v.stride(-2) == V, "v heads must be contiguous")
+    _require(checkpoint_state.ndim == 4, "checkpoint must be four-dimensional")
+    nb = checkpoint_state.shape[0]
+    _require(tuple(checkpoint_state.shape[1:]) == (HV, V, K), "checkpoint shape is incompatible")
+    _require(K == V and K in SUPPORTED_HEAD_DIMS, f"K and V must be equal and one of {SUPPORTED_HEAD_DIMS}")
+    _require(g2.dtype == torch.float32, "gate must be FP32 log-space decay")
+    _require(beta2.dtype in (torch.float32, q.dtype), "beta must be FP32 or the activation dtype")
+    _require(q.dtype in (torch.float32, torch.bfloat16, torch.float16) and k.dtype == q.dtype and v.dtype == q.dtype,
+             "q/k/v must share one FP32/BF16/FP16 dtype")
+    _require(checkpoint_state.dtype == torch.float32 or (checkpoint_state.dtype == torch.bfloat16 and K >= 64),
+             "checkpoint must be FP32 (or BF16 with K >= 64)")
+    soa = isinstance(replay_cache, ReplayRecordBuffers)
+    if soa:
+        corr, key_record, decay_record = replay_cache.correction, replay_cache.key, replay_cache.decay
+        _require(
+            corr.ndim == 4
+            and tuple(corr.shape[1:]) == (HV, spec_query_len, V)
+            and tuple(key_record.shape) == (corr.shape[0], H, spec_query_len, K)
+            and tuple(decay_record.shape) == (corr.shape[0], HV, spec_query_len),
+            "typed record geometry is incompatible",
+        )
+        _require(corr.dtype == decay_record.dtype == torch.float32, "correction and decay records must remain FP32")
+        _require(
+            key_record.dtype in (torch.float16, torch.bfloat16, torch.float32)
+            and (key_record.dtype == torch.float32 or (qk_already_normalized and key_record.dtype == k.dtype)),
+            "low-precision key records require already-normalized input dtype",
+        )
+        _require(all(t.stride(-1) == 1 for t in (corr, key_record, decay_record)),
+                 "typed record innermost dimensions must be contiguous")
+        key_strides = tuple(key_record.stride()[:3])
+        decay_strides = tuple(decay_record.stride())
+    else:
+        corr = key_record = decay_record = replay_cache
+        _require(corr.ndim == 4 and tuple(corr.shape[1:]) == (HV, spec_query_len, V + K + 1),
+                 "packed replay record shape is incompatible")
+        _require(corr.dtype == torch.float32, "packed records must remain FP32")
+        _require(corr.stride(-1) == 1, "packed record innermost dimension must be contiguous")
+        key_strides = tuple(corr.stride()[:3])
+        decay_strides = tuple(corr.stride()[:3])
+    _require(corr.shape[0] >= 1, "replay buffer has no rows")
+    _require(state_indices.ndim == 1, "state indices must be one-dimensional")
+    _require(query_start_loc.ndim == 1 and query_start_loc.shape[0] == state_indices.shape[0] + 1,
+             "query metadata is incompatible")
+    _require(total <= state_indices.shape[0] * spec_query_len, "speculative decode input exceeds its activation capacity")
+    _require(query_start_loc.dtype in (torch.int32, torch.int64) and state_indices.dtype in (torch.int32, torch.int64),
+             "query metadata must be int32 or int64")
+    dev = q.device
+    _require(
+        all(t_.device == dev for t_ in (k, v, g, beta, checkpoint_state, corr, key_record, decay_record,
+                                         query_start_loc, state_indices))
+        and (out is None or out.device == dev),
+        "inputs must be on the same device",
+    )
+    if scale is None:
+        scale = K**-0.5
+    if out is None:
+        out = torch.empty(1, total, HV, V, dtype=v.dtype, device=v.device)
+    _require(tuple(out.shape) == (1, total, HV, V) and out.stride()[2:] == (V, 1) and out.dtype == v.dtype,
+             "output shape or layout is incompatible")
+    batch = state_indices.shape[0]
+    if total == 0 or batch == 0:
+        return out
+    config = [
+        batch, total, H, HV, spec_query_len, nb, corr.shape[0], NULL_BLOCK_ID,
+        q.stride(1), k.stride(1), v.stride(1), g2.stride(0), beta2.stride(0),
+        checkpoint_state.stride(0), checkpoint_state.stride(1), checkpoint_state.stride(2),
+        corr.stride(0), corr.stride(1), corr.stride(2),
+        *key_strides, *decay_strides,
+        out.stride(1), query_start_loc.stride(0), state_indices.stride(0),
+    ]
+    flags = (0 if soa else _RECORD_PACKED) | (0 if qk_already_normalized else _NORMALIZE_QK)
+    spec = _LaunchSpec(
+        "verify",
+        _native.ops().verify_ext,
+        (q, k, v, g2, beta2, checkpoint_state, corr, key_record, decay_record, out, query_start_loc,
+         state_indices, config, float(scale), flags),
+    )
+    if _collect is None:
+        spec.launch()
+    else:
+        _collect.append(spec)
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# per-context commit
+# --------------------------------------------------------------------------- #
+@dataclass
+class GDNRecoverSSMCommitContext:
+    """Per-layer-set commit state: address/stride tables of every layer's
+    checkpoint pool, conv pool and records, plus reusable plan buffers
+    (kernels.py:1399-2052).  Build with ``from_tensors``."""
+
+    conv_states: tuple
+    conv_state_base_addrs: torch.Tensor
+    conv_state_block_strides: torch.Tensor
+    conv_state_dim_strides: torch.Tensor
+    conv_state_token_strides: torch.Tensor
+    conv_history_len: int
+    checkpoints: tuple
+    state_base_addrs: torch.Tensor
+    state_block_strides: torch.Tensor
+    replays: tuple
+    replay_base_addrs: torch.Tensor
+    replay_block_strides: torch.Tensor
+    commit_lens: torch.Tensor
+    final_state_indices: torch.Tensor
+    boundary_state_indices: torch.Tensor
+    boundary_recovery_lens: torch.Tensor
+    spec_query_len: int
+    num_blocks: int
+
+    @classmethod
+    def from_tensors(cls, conv_states, checkpoints, replays, *, spec_query_len: int, max_num_reqs: int,
+                     conv_dim_first: bool = True) -> "GDNRecoverSSMCommitContext":
+        """Validate every layer's page layout and build the int64 address /
+        stride tables and plan buffers (kernels.py:1421-1565)."""
+        _require(len(checkpoints) > 0, "commit requires at least one layer")
+        _require(len(conv_states) == len(checkpoints) == len(replays), "conv, state and replay lists differ")
+        _require(0 < spec_query_len <= MAX_SPEC_QUERY_LEN, f"spec_query_len must be in [1, {MAX_SPEC_QUERY_LEN}]")
+        if not conv_dim_first:
+            conv_states = [s.transpose(-1, -2) for s in conv_states]
+        ref = checkpoints[0]
+        _require(ref.ndim == 4, "checkpoint must be four-dimensional")
+        nb, HV, V, K = ref.shape
+        dev = ref.device
+        for s in checkpoints:
+            _require(
+                s.shape == ref.shape and s.dtype == ref.dtype and s.stride()[1:] == ref.stride()[1:] and s.device == dev,
+                "layers need matching checkpoints",
+            )
+        soa = isinstance(replays[0], ReplayRecordBuffers)
+        _require(all(isinstance(r, ReplayRecordBuffers) == soa for r in replays),
+                 "packed and typed records cannot share a commit context")
+        if soa:
+            corrs = [r.correction for r in replays]
+            keys = [r.key for r in replays]
+            decays = [r.decay for r in replays]
+            H = keys[0].shape[1]
+            _require(H > 0 and HV % H == 0, "record key heads are incompatible")
+            for c, k, d in zip(corrs, keys, decays):
+                _require(
+                    c.shape == corrs[0].shape
+                    and tuple(c.shape[1:]) == (HV, spec_query_len, V)
+                    and tuple(k.shape) == (c.shape[0], H, spec_query_len, K)
+                    and tuple(d.shape) == (c.shape[0], HV, spec_query_len)
+                    and c.dtype == d.dtype == torch.float32
+                    and k.dtype in (torch.float16, torch.bfloat16, torch.float32)
+                    and k.dtype == keys[0].dtype
+                    and all(t.device == dev for t in (c, k, d))
+                    and c.stride()[1:] == corrs[0].stride()[1:]
+                    and k.stride()[1:] == keys[0].stride()[1:]
+                    and d.stride()[1:] == decays[0].stride()[1:],
+                    "layers need matching typed replay geometry/dtypes/strides",
+                )
+        else:
+            corrs = keys = decays = list(replays)
+            H = HV
+            for r in replays:
+                _require(
+                    r.ndim == 4
+                    and tuple(r.shape[1:]) == (HV, spec_query_len, V + K + 1)
+                    and r.shape == replays[0].shape
+                    and r.dtype == torch.float32
+                    and r.stride()[1:] == replays[0].stride()[1:]
+                    and r.device == dev,
+                    "layers need matching packed FP32 replay buffers",
+                )
+        conv_ref = conv_states[0]
+        _require(conv_ref.ndim == 3 and conv_ref.shape[0] == nb,
+                 "conv state must be [blocks, dim, window] with the checkpoint's block count")
+        for c in conv_states:
+            _require(
+                c.shape == conv_ref.shape and c.dtype == conv_ref.dtype and c.stride()[1:] == conv_ref.stride()[1:]
+                and c.device == dev,
+                "layers need matching conv states",
+            )
+        conv_dim, conv_len = conv_ref.shape[1:]
+        hist = conv_len - spec_query_len + 1
+        _require(hist > 0, "conv state is shorter than its window")
+
+        def strides(ts, dim):
+            return torch.tensor([t.stride(dim) for t in ts], dtype=torch.int64, device=dev)
+
+        def plan_buf():
+            return torch.zeros(max_num_reqs, dtype=torch.int32, device=dev)
+
+        context = cls(
+            tuple(conv_states),
+            _ptr_table(conv_states, dev),
+            strides(conv_states, 0),
+            strides(conv_states, 1),
+            strides(conv_states, 2),
+            hist,
+            tuple(checkpoints),
+            _ptr_table(checkpoints, dev),
+            strides(checkpoints, 0),
+            tuple(replays),
+            _ptr_table(corrs, dev),
+            strides(corrs, 0),
+            plan_buf(),
+            plan_buf(),
+            plan_buf(),
+            plan_buf(),
+            spec_query_len,
+            nb,
+        )
+        context.records = list(replays)
+        context.record_rows = int(corrs[0].shape[0])
+        context.record_layout = "soa" if soa else "packed"
+        context.num_key_heads = int(H)
+        context.key_dtype = keys[0].dtype
+        context.correction_base_addrs = context.replay_base_addrs
+        context.correction_block_strides = context.replay_block_strides
+        context.key_base_addrs = _ptr_table(keys, dev)
+        context.key_block_strides = strides(keys, 0)
+        context.decay_base_addrs = _ptr_table(decays, dev)
+        context.decay_block_strides = strides(decays, 0)
+        context.record_bytes = sum(record_nbytes(r) for r in replays)
+        context.align_valid = plan_buf()
+        context.align_col = plan_buf()
+        context.layer_groups = torch.zeros(len(checkpoints), dtype=torch.int32, device=dev)
+        return context
+
+    def make_commit_specs(self, num_accepted_tokens, state_indices, query_start_loc, request_indices=None,
+                          block_table=None, num_computed_tokens=None, mamba_block_size=None,
+                          commit_conv=True) -> tuple:
+        """The launch specs of one step, without launching them (kernels.py:1648-1676)."""
+        specs: list[_LaunchSpec] = []
+        self.commit(num_accepted_tokens, state_indices, query_start_loc, request_indices=request_indices,
+                    block_table=block_table, num_computed_tokens=num_computed_tokens,
+                    mamba_block_size=mamba_block_size, commit_conv=commit_conv, _collect=specs)
+        return tuple(specs)
+
+    def commit(self, num_accepted_tokens, state_indices, query_start_loc, request_indices=None, block_table=None,
+               num_computed_tokens=None, mamba_block_size=None, commit_conv=True, _collect=None) -> None:
+        """Fold each row's accepted prefix into every layer's checkpoint and
+        compact the conv history: plan -> conv -> fold on the current stream
+        (kernels.py:1823-2052).  In align mode (block table, computed counts
+        and block size given) the state lands in the block holding the last
+        committed token and a crossed block boundary is snapshotted mid-fold."""
+        batch = state_indices.shape[0]
+        if batch == 0:
+            return
+        _require(state_indices.ndim == 1, "state indices must be one-dimensional")
+        _require(batch <= self.commit_lens.shape[0], "commit batch exceeds its plan capacity")
+        _require(query_start_loc.ndim == 1 and query_start_loc.shape[0] == batch + 1, "commit metadata is incompatible")
+        _require(request_indices is None or request_indices.shape[0] >= batch, "request mapping is too short")
+        _require(num_accepted_tokens.ndim == 1 and (request_indices is not None or num_accepted_tokens.shape[0] >= batch),
+                 "accepted-token counts are too short")
+        align_args = (block_table, num_computed_tokens, mamba_block_size)
+        _require(all(x is None for x in align_args) or all(x is not None for x in align_args),
+                 "align metadata is incomplete")
+        _require(mamba_block_size is None or mamba_block_size >= self.spec_query_len,
+                 "align block size must cover one speculative window")
+        _require(block_table is None or (block_table.ndim == 2 and block_table.shape[1] > 0),
+                 "block table must be two-dimensional with a positive width")
+        dev = self.checkpoints[0].device
+        _require(
+            all(t_ is None or t_.device == dev for t_ in (num_accepted_tokens, state_indices, query_start_loc,
+                                                         request_indices, block_table, num_computed_tokens)),
+            "commit inputs must be on the same device",
+        )
+        ops = _native.ops()
+        specs = []
+        specs.append(_LaunchSpec(
+            "commit_plan", ops.commit_plan,
+            (num_accepted_tokens, request_indices, state_indices, query_start_loc, block_table, num_computed_tokens,
+             self.commit_lens, self.final_state_indices, self.boundary_state_indices, self.boundary_recovery_lens,
+             self.align_valid, self.align_col, self.spec_query_len, self.num_blocks, int(mamba_block_size or 1)),
+        ))
+        layers = len(self.checkpoints)
+        if commit_conv:
+            conv = self.conv_states[0]
+            specs.append(_LaunchSpec(
+                "compact_conv", ops.compact_conv,
+                (conv, self.conv_state_base_addrs, self.conv_state_block_strides, self.conv_state_dim_strides,
+                 self.conv_state_token_strides, self.layer_groups, state_indices, self.commit_lens,
+                 self.final_state_indices, self.boundary_state_indices, self.boundary_recovery_lens, batch,
+                 self.commit_lens.shape[0], int(conv.shape[1]), self.conv_history_len, int(conv.shape[2]),
+                 self.num_blocks, block_table is not None),
+            ))
+        ref = self.checkpoints[0]
+        _, HV, V, K = ref.shape
+        soa = self.record_layout == "soa"
+        record = self.replays[0]
+        rr = record.correction if soa else record
+        kr = record.key if soa else record
+        dr = record.decay if soa else record
+        config = [
+            batch, layers, HV, self.num_key_heads, self.spec_query_len, self.num_blocks, rr.shape[0],
+            self.commit_lens.shape[0], NULL_BLOCK_ID, ref.stride(1), ref.stride(2), rr.stride(1), rr.stride(2),
+            kr.stride(1) if soa else 0, kr.stride(2) if soa else 0, dr.stride(1) if soa else 0,
+            dr.stride(2) if soa else 0,
+        ]
+        specs.append(_LaunchSpec(
+            "fold", ops.fold_ext,
+            (ref, rr, kr, dr, self.state_base_addrs, self.state_block_strides, self.correction_base_addrs,
+             self.correction_block_strides, self.key_base_addrs, self.key_block_strides, self.decay_base_addrs,
+             self.decay_block_strides, self.layer_groups, state_indices, self.commit_lens, self.final_state_indices,
+             self.boundary_state_indices, self.boundary_recovery_lens, config, 0 if soa else _FOLD_PACKED),
+        ))
+        if _collect is not None:
+            _collect.extend(specs)
+            return
+        for spec in specs:
+            spec.launch()
+        self._last_specs = tuple(specs)
+
+
+__all__ = [
+    "GDNRecoverSSMCommitContext",
+    "ReplayRecordBuffers",
+    "gdn_recoverssm_verify",
+    "record_geometry_bytes",
+    "record_nbytes",
+    "MAX_SPEC_QUERY_LEN",
+    "NULL_BLOCK_ID",
+]

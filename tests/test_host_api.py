@@ -1,0 +1,278 @@
+"""Host-side contract tests (CPU only): the C ABI library loads and exports
+every entry point the header declares, rejects bad arguments before any launch
+(no GPU needed), and the Python entry points keep the reference's
+signatures, ValueError checks and byte accounting."""
+
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "gdn_recoverssm_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return re.findall(r"GDN_RSSM_API\s+[\w\s\*]+?\b(gdn_rssm_\w+)\s*\(", text)
+
+
+def test_library_exports_every_declared_symbol():
+    from gdn_recoverssm_b200 import capi
+
+    names = _declared()
+    assert len(names) == 9, names
+    lib = capi.lib()
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(capi.PROTOTYPES)
+    assert lib.gdn_rssm_abi_version() == 1
+
+
+def test_torch_ops_register_reference_schemas():
+    from gdn_recoverssm_b200 import _native
+
+    ops = _native.ops()
+    assert ops.abi_version() == 1
+    verify = str(ops.verify.default._schema)
+    fold = str(ops.fold.default._schema)
+    # the reference's native schemas (csrc/ops.cpp:243-251), argument for argument
+    assert verify == (
+        "gdn_recoverssm_ac::verify(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor state, "
+        "Tensor(a!) correction, Tensor(b!) key, Tensor(c!) decay, Tensor(d!) out, Tensor qsl, Tensor indices, "
+        "int[] config, float scale) -> ()"
+    )
+    assert fold.startswith("gdn_recoverssm_ac::fold(Tensor(a!) state, Tensor correction, Tensor key, Tensor decay,")
+    assert fold.endswith("Tensor boundary_lengths, int[] config) -> ()")
+
+
+def _verify_call(lib, capi, config, **over):
+    args = dict(act=capi.BF16, state=capi.F32, beta=capi.F32, key=capi.F32, qsl=capi.I32, idx=capi.I32, K=128, V=128,
+                flags=capi.RECORD_PACKED)
+    args.update(over)
+    cfg = capi.int64_array(config)
+    return lib.gdn_rssm_verify(*([None] * 12), cfg, len(config), 1.0, args["act"], args["state"], args["beta"],
+                               args["key"], args["qsl"], args["idx"], args["K"], args["V"], args["flags"], None)
+
+
+def _good_config():
+    # rows, tokens, H, HV, Q, blocks, record_rows, null, ... strides
+    return [4, 16, 2, 4, 4, 8, 4, 0] + [1] * 20
+
+
+@pytest.mark.parametrize(
+    "mutate,over,match",
+    [
+        (lambda c: c[:27], {}, "28 fields"),
+        (lambda c: c[:7] + [1] + c[8:], {}, "null block"),
+        (lambda c: c, {"K": 64}, "K and V must be equal"),
+        (lambda c: c, {"K": 96, "V": 96}, "K and V must be equal"),
+        (lambda c: c[:4] + [9] + c[5:], {}, "spec_query_len"),
+        (lambda c: c[:2] + [3] + c[3:], {}, "multiple"),
+        (lambda c: c, {"beta": 2}, "beta"),
+        (lambda c: c, {"flags": 0, "key": 1, "act": 0}, "low-precision key"),
+        (lambda c: c, {"state": 2}, "state must be"),
+        (lambda c: c[:1] + [100] + c[2:], {}, "activation capacity"),
+    ],
+)
+def test_capi_verify_rejects_before_launch(mutate, over, match):
+    from gdn_recoverssm_b200 import capi
+
+    lib = capi.lib()
+    rc = _verify_call(lib, capi, mutate(_good_config()), **over)
+    assert rc == capi.EINVAL
+    assert match in capi.last_error()
+
+
+def test_capi_fold_and_plans_reject_before_launch():
+    from gdn_recoverssm_b200 import capi
+
+    lib = capi.lib()
+    cfg = capi.int64_array([4] * 16)
+    rc = lib.gdn_rssm_fold(*([None] * 9), capi.index_view(None), *([None] * 4), 0, cfg, 16, capi.F32, capi.F32, 128,
+                           128, 0, None)
+    assert rc == capi.EINVAL and "17 fields" in capi.last_error()
+    group = capi.PlanGroup()
+    rc = lib.gdn_rssm_grouped_plan(capi.index_view(None), group, 4, *([None] * 7), capi.index_view(None),
+                                   capi.out_view(None), capi.out_view(None), 2, 8, 4, 0, 1, 1, None)
+    assert rc == capi.EINVAL and "one to three groups" in capi.last_error()
+    rc = lib.gdn_rssm_commit_plan(*([capi.index_view(None)] * 4), capi.table_view(None), capi.index_view(None),
+                                  *([None] * 6), 2, 9, 16, 4, 0, None)
+    assert rc == capi.EINVAL and "plan geometry" in capi.last_error()
+    rc = lib.gdn_rssm_compact_conv(*([None] * 5), capi.index_view(None), *([None] * 4), 1, 2, 1, 4, 16, 3, 2, 8, 0,
+                                   capi.F32, 0, None)
+    assert rc == capi.EINVAL and "window" in capi.last_error()
+
+
+# ---- Python entry points -------------------------------------------------- #
+def test_record_geometry_bytes_matches_reference_deployment():
+    from gdn_recoverssm_b200 import kernels
+
+    kw = dict(rows=128, num_layers=48, num_value_heads=12, num_key_heads=4, window=4, key_dim=128, value_dim=128)
+    # reference test_record_buffers.py:112-137: deployed TP4 geometry
+    assert kernels.record_geometry_bytes(**kw, key_dtype=torch.float32) == 193.125 * 1024**2
+    assert kernels.record_geometry_bytes(**kw, key_dtype=torch.bfloat16) == 169.125 * 1024**2
+    rec = kernels.ReplayRecordBuffers.allocate(3, 6, 2, 4, 8, 8, device="cpu", key_dtype=torch.bfloat16)
+    assert rec.shape == (3, 6, 4, 17)
+    assert kernels.record_nbytes(rec) == kernels.record_geometry_bytes(3, 1, 6, 2, 4, 8, 8, torch.bfloat16)
+    with pytest.raises(ValueError, match="GDN RecoverSSM: record head/row geometry is invalid"):
+        kernels.ReplayRecordBuffers.allocate(3, 6, 4, 4, 8, 8, device="cpu")
+
+
+def _verify_inputs(T=8, H=2, HV=4, D=32, Q=4):
+    return dict(
+        g=torch.zeros(1, T, HV), beta=torch.ones(1, T, HV), q=torch.zeros(1, T, H, D, dtype=torch.bfloat16),
+        k=torch.zeros(1, T, H, D, dtype=torch.bfloat16), v=torch.zeros(1, T, HV, D, dtype=torch.bfloat16),
+        checkpoint_state=torch.zeros(5, HV, D, D), replay_cache=torch.zeros(2, HV, Q, 2 * D + 1),
+        query_start_loc=torch.tensor([0, 4, 8], dtype=torch.int32),
+        state_indices=torch.tensor([1, 2], dtype=torch.int32), spec_query_len=Q,
+    )
+
+
+@pytest.mark.parametrize(
+    "change,match",
+    [
+        (dict(q=torch.zeros(8, 2, 32)), "q must have shape"),
+        (dict(spec_query_len=9), r"spec_query_len must be in \[1, 8\]"),
+        (dict(replay_cache=torch.zeros(2, 4, 4, 64)), "packed replay record shape"),
+        (dict(checkpoint_state=torch.zeros(5, 4, 32, 16)), "checkpoint shape is incompatible"),
+        (dict(query_start_loc=torch.tensor([0, 4], dtype=torch.int32)), "query metadata is incompatible"),
+        (dict(g=torch.zeros(1, 7, 4)), "gate or beta shape"),
+        (dict(replay_cache=torch.zeros(2, 4, 4, 65, dtype=torch.float16)), "packed records must remain FP32"),
+    ],
+)
+def test_verify_argument_errors_raise_before_launch(change, match):
+    from gdn_recoverssm_b200 import gdn_recoverssm_verify
+
+    kw = _verify_inputs()
+    kw.update(change)
+    g, beta, q, k, v = (kw.pop(n) for n in ("g", "beta", "q", "k", "v"))
+    with pytest.raises(ValueError, match="GDN RecoverSSM: " + match):
+        gdn_recoverssm_verify(g, beta, q, k, v, **kw)
+
+
+def test_verify_collects_one_native_launch_without_running_it():
+    from gdn_recoverssm_b200 import gdn_recoverssm_verify
+
+    kw = _verify_inputs()
+    g, beta, q, k, v = (kw.pop(n) for n in ("g", "beta", "q", "k", "v"))
+    specs = []
+    out = gdn_recoverssm_verify(g, beta, q, k, v, _collect=specs, **kw)
+    assert out.shape == (1, 8, 4, 32) and len(specs) == 1 and specs[0].name == "verify"
+    config = specs[0].args[12]
+    assert len(config) == 28 and config[:8] == [2, 8, 2, 4, 4, 5, 2, 0]
+
+
+def test_cpu_tensors_fail_loudly_in_the_native_op():
+    """No CPU fallback: the op refuses non-CUDA tensors."""
+    from gdn_recoverssm_b200 import gdn_recoverssm_verify
+
+    kw = _verify_inputs()
+    g, beta, q, k, v = (kw.pop(n) for n in ("g", "beta", "q", "k", "v"))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        gdn_recoverssm_verify(g, beta, q, k, v, **kw)
+
+
+def _context(g, *, soa=True, dtype=torch.bfloat16, blocks=64, layers=2):
+    states = [torch.zeros(blocks, 6, 32, 32) for _ in range(layers)]
+    convs = [torch.zeros(blocks, 32, 6, dtype=dtype) for _ in range(layers)]
+    if soa:
+        recs = [g.ReplayRecordBuffers.allocate(8, 6, 2, 4, 32, 32, device="cpu", key_dtype=dtype) for _ in range(layers)]
+    else:
+        recs = [torch.zeros(8, 6, 4, 65) for _ in range(layers)]
+    return g.GDNRecoverSSMCommitContext.from_tensors(convs, states, recs, spec_query_len=4, max_num_reqs=8)
+
+
+def test_context_tables_and_validation():
+    import gdn_recoverssm_b200 as g
+
+    ctx = _context(g)
+    assert ctx.conv_history_len == 3 and ctx.num_blocks == 64 and ctx.record_layout == "soa"
+    assert ctx.state_base_addrs.tolist() == [s.data_ptr() for s in ctx.checkpoints]
+    assert ctx.key_block_strides.tolist() == [2 * 4 * 32] * 2
+    assert ctx.num_key_heads == 2 and ctx.record_rows == 8
+    with pytest.raises(ValueError, match="packed and typed records cannot share"):
+        g.GDNRecoverSSMCommitContext.from_tensors(
+            [torch.zeros(8, 32, 6)] * 2, [torch.zeros(8, 6, 32, 32)] * 2,
+            [torch.zeros(8, 6, 4, 65), g.ReplayRecordBuffers.allocate(8, 6, 2, 4, 32, 32, device="cpu")],
+            spec_query_len=4, max_num_reqs=8)
+    with pytest.raises(ValueError, match="conv state is shorter than its window"):
+        g.GDNRecoverSSMCommitContext.from_tensors(
+            [torch.zeros(8, 32, 3)], [torch.zeros(8, 6, 32, 32)], [torch.zeros(8, 6, 4, 65)], spec_query_len=4,
+            max_num_reqs=8)
+    specs = ctx.make_commit_specs(torch.ones(2, dtype=torch.int32), torch.tensor([1, 2], dtype=torch.int32),
+                                  torch.tensor([0, 4, 8], dtype=torch.int32))
+    assert [s.name for s in specs] == ["commit_plan", "compact_conv", "fold"]
+    with pytest.raises(ValueError, match="align metadata is incomplete"):
+        ctx.commit(torch.ones(2, dtype=torch.int32), torch.tensor([1, 2], dtype=torch.int32),
+                   torch.tensor([0, 4, 8], dtype=torch.int32), block_table=torch.zeros(2, 4, dtype=torch.int32))
+
+
+def _entry(g, context, group=0, align=True):
+    from types import SimpleNamespace
+
+    p = SimpleNamespace(
+        state_indices=torch.tensor([8, 4], dtype=torch.int32), query_start_loc=torch.tensor([0, 4, 8], dtype=torch.int32),
+        request_indices=torch.tensor([2, 0], dtype=torch.int64),
+        block_table=(torch.arange(12, dtype=torch.int32).reshape(3, 4) + 2 + 20 * group) if align else None,
+        num_computed_tokens=torch.tensor([3, 0, 7], dtype=torch.int32) if align else None, block_size=4 if align else None,
+        request_rows=(2, 0), query_lens=(4, 4),
+    )
+    meta = SimpleNamespace(recoverssm_commit=p, recoverssm_builder=SimpleNamespace(), recoverssm_context=context)
+    return g.CommitEntry(meta, p, context)
+
+
+def _inputs():
+    return (torch.tensor([1, 0, 3], dtype=torch.int32), torch.tensor([5, -1, 1], dtype=torch.int32),
+            torch.full((6,), -9, dtype=torch.int32), torch.full((6,), 7, dtype=torch.int32))
+
+
+def test_bucket_builds_three_specs_and_rejects_bad_steps():
+    import gdn_recoverssm_b200 as g
+
+    ctxs = [_context(g) for _ in range(3)]
+    entries = [_entry(g, c, i) for i, c in enumerate(ctxs)]
+    bucket = g.GroupedCommitBucket(ctxs)
+    assert bucket.layer_groups.tolist() == [0, 0, 1, 1, 2, 2] and bucket.capacity == 8
+    specs = bucket.make_specs(entries, *_inputs())
+    assert [s.name for s in specs] == ["grouped_plan", "compact_conv", "fold"]
+    sampled, mapping, cols, acc = _inputs()
+    with pytest.raises(ValueError, match="must not alias"):
+        bucket.make_specs(entries, sampled, mapping, cols, sampled)
+    with pytest.raises(ValueError, match="different KV epoch"):
+        bucket.make_specs([_entry(g, _context(g))] * 3, *_inputs())
+    with pytest.raises(ValueError, match="homogeneous layer layouts"):
+        g.GroupedCommitBucket([_context(g), _context(g, dtype=torch.float32)])
+    with pytest.raises(ValueError, match="one to three contexts"):
+        g.GroupedCommitBucket([_context(g) for _ in range(4)])
+
+
+def test_coordinator_buckets_and_publication_counts(monkeypatch):
+    import gdn_recoverssm_b200 as g
+    from gdn_recoverssm_b200 import kernels
+
+    launched = []
+    monkeypatch.setattr(kernels._LaunchSpec, "launch", lambda self: launched.append(self.name))
+    coord = g.GroupedCommitCoordinator()
+    ctxs = [_context(g) for _ in range(3)]
+    entries = [_entry(g, c, i) for i, c in enumerate(ctxs)]
+    coord.commit([e.metadata for e in entries], *_inputs())
+    assert coord.last_group_count == 3 and coord.last_launch_count == 3
+    first = next(iter(coord._buckets.values()))
+    coord.commit([e.metadata for e in entries], *_inputs())
+    assert next(iter(coord._buckets.values())) is first
+    # seven homogeneous groups: buckets of 3 + 3 + 1 plus one AND-valid publication
+    seven = [_entry(g, _context(g), i % 2) for i in range(7)]
+    launched.clear()
+    coord.commit([e.metadata for e in seven], *_inputs())
+    assert coord.last_launch_count == 10 and launched[-1] == "publish_align"
+    assert [len(b.contexts) for b in coord._buckets.values()] == [3, 3, 1]
+    # heterogeneous layouts: separate buckets
+    mixed = [_entry(g, _context(g)), _entry(g, _context(g, dtype=torch.float32), 1)]
+    coord.commit([e.metadata for e in mixed], *_inputs())
+    assert coord.last_launch_count == 7 and len(coord._buckets) == 2
+    bad = [_entry(g, _context(g)), _entry(g, _context(g), 1)]
+    bad[1].payload.block_size = 8
+    with pytest.raises(ValueError, match="must agree"):
+        coord.commit([e.metadata for e in bad], *_inputs())
