@@ -157,9 +157,13 @@ def run_reference(args):
     from gdn_recoverssm_b200 import synthetic
 
     spec = synthetic.CONFIGS[args.config]
-    rows = args.cpu_rows
-    for _ in range(max(args.warmup, 0) and 1):
-        cpu_baseline(args.config, rows_sample=max(1, rows // 8))
+    # size each step's sample so that warm-up + K steps fit the time budget
+    probe = cpu_baseline(args.config, rows_sample=4)
+    per_row = probe["seconds_per_sample"] / 4
+    budget = args.reference_budget_s / max(1, args.steps + min(args.warmup, 1))
+    rows = int(max(1, min(spec["B"], budget / per_row)))
+    if args.warmup > 0:
+        cpu_baseline(args.config, rows_sample=rows)
     vals = []
     for _ in range(args.steps):
         vals.append(cpu_baseline(args.config, rows_sample=rows)["value"])
@@ -206,7 +210,7 @@ def run_b200(args):
     from gdn_recoverssm_b200 import _native, synthetic
 
     _native.ops()
-    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=16)
+    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=16, rows=args.rows, pool=args.pool)
     stream = torch.cuda.current_stream(dev)
     ctx = g.GDNRecoverSSMCommitContext.from_tensors([wl.conv], [wl.state], [wl.records], spec_query_len=wl.Q,
                                                     max_num_reqs=wl.B)
@@ -349,12 +353,16 @@ def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier):
 def main(argv=None):
     ap = argparse.ArgumentParser(description="RecoverSSM verify+commit benchmark")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-rows", type=int, default=16, help="rows in the CPU baseline's bounded sample")
+    ap.add_argument("--cpu-rows", type=int, default=512, help="rows in the CPU baseline's bounded sample")
+    ap.add_argument("--reference-budget-s", type=float, default=60.0,
+                    help="CPU seconds the --impl reference run may spend over all its steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=None, help="reduced batch (profiling cases only)")
+    ap.add_argument("--pool", type=int, default=None, help="reduced state pool (profiling cases only)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

@@ -148,6 +148,19 @@ __device__ __forceinline__ int64_t floordiv(int64_t a, int64_t b) {
   return q;
 }
 
+// SM count of the current device (cached per device).
+inline int sm_count_current_device() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (counts[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
 // Host helpers.
 bool host_dtype_is_float(int32_t d);
 int host_dtype_size(int32_t d);

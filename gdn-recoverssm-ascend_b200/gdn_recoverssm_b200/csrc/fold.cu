@@ -13,8 +13,21 @@ int launch_fold_variant(FoldParams p, cudaStream_t stream) {
     set_error("GDN RecoverSSM: cannot resolve the device status word");
     return GDN_RSSM_ECUDA;
   }
+  constexpr int smem = fold_smem_bytes<DIM, St>();
+  static bool configured[64] = {false};
+  int dev = 0;
+  GDN_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_error("GDN RecoverSSM: device ordinal out of range");
+    return GDN_RSSM_EUNSUPPORTED;
+  }
+  if (!configured[dev]) {
+    GDN_CUDA(cudaFuncSetAttribute(fold_kernel<DIM, St, Kt>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured[dev] = true;
+  }
+  // one CTA per (layer, row, value head) unit
   const int64_t grid = p.layers * p.rows * p.heads;
-  fold_kernel<DIM, St, Kt><<<static_cast<unsigned>(grid), kFoldThreads, 0, stream>>>(p);
+  fold_kernel<DIM, St, Kt><<<static_cast<unsigned>(grid), kFoldThreads, smem, stream>>>(p);
   GDN_CUDA(cudaGetLastError());
   return GDN_RSSM_OK;
 }

@@ -10,19 +10,24 @@
 //     store h to the final page.
 // The update is the reference's exact arithmetic order (tl.fma(c, k, h*d)).
 //
-// B200 design.  Pure HBM streaming: one CTA per unit, each thread owns a fixed
-// 16-byte column chunk (so its key slice lives in registers for the whole
-// window) and a strided set of rows; all of a thread's state chunks are
-// loaded before any is folded, so ~64 KiB per CTA is in flight.  The corr
-// vectors of the window are staged in shared memory and read as broadcasts.
-// Every element is read and written by the same thread, so in-place commits
-// and a boundary page that aliases the source page are race-free.
+// B200 design: one CTA (256 threads) per unit, three resident per SM.  Thread
+// 0 starts one bulk copy (cp.async.bulk, completion on an mbarrier) of the
+// source state tile into shared memory -- 64 KiB in flight per CTA without
+// holding registers -- while all threads stage the window's corr / decay
+// records in shared memory and their key slice in registers (each thread
+// owns one 16-byte column chunk of the tile and a strided set of rows).  The
+// fold then streams the final state, and the boundary snapshot mid-fold,
+// straight to HBM with 16-byte stores.  The whole source tile is in shared
+// memory before any store of the unit, so in-place commits and a boundary
+// page that aliases the source page are safe.
 #pragma once
 
 #include "params.cuh"
+#include "ptx.cuh"
 
 namespace gdn_rssm {
 
+constexpr uint64_t kFoldWaitLimitNs = 1000000000ull;  // 1 s
 
 template <typename T>
 struct Chunk16 {
@@ -43,16 +48,6 @@ __device__ __forceinline__ void unpack16(const uint4 raw, float *out, __nv_bfloa
     out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
   }
 }
-__device__ __forceinline__ void unpack16(const uint4 raw, float *out, __half) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 hh = *reinterpret_cast<const __half2 *>(&w[i]);
-    const float2 f = __half22float2(hh);
-    out[2 * i] = f.x;
-    out[2 * i + 1] = f.y;
-  }
-}
 
 __device__ __forceinline__ uint4 pack16(const float *in, float) {
   return make_uint4(__float_as_uint(in[0]), __float_as_uint(in[1]), __float_as_uint(in[2]), __float_as_uint(in[3]));
@@ -67,15 +62,41 @@ __device__ __forceinline__ uint4 pack16(const float *in, __nv_bfloat16) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <int DIM, typename St, typename Kt>
-__global__ void __launch_bounds__(kFoldThreads, 2) fold_kernel(const FoldParams p) {
-  constexpr int EPC = Chunk16<St>::N;      // state elements per 16-B chunk
-  constexpr int CPR = DIM / EPC;           // chunks per state row
-  constexpr int RSTEP = kFoldThreads / CPR;  // rows between a thread's chunks
-  constexpr int CPT = (DIM + RSTEP - 1) / RSTEP;  // chunks per thread (last may be empty)
+template <int DIM, typename St>
+struct FoldShape {
+  static constexpr int EPC = Chunk16<St>::N;             // state elements per 16-byte chunk
+  static constexpr int CPR = DIM / EPC;                  // chunks per state row
+  static constexpr int RSTEP = kFoldThreads / CPR;       // rows between a thread's chunks
+  static constexpr int CPT = (DIM + RSTEP - 1) / RSTEP;  // chunks per thread (last may be empty)
+  static constexpr int TILE = DIM * DIM * sizeof(St);
+  static constexpr int CORR = kMaxWindow * DIM * 4;
+  static constexpr int SMEM = 128 /* alignment slack */ + TILE + CORR + 64;
   static_assert(kFoldThreads % CPR == 0, "fold layout");
-  __shared__ float s_corr[kMaxWindow][DIM];
-  __shared__ float s_decay[kMaxWindow];
+};
+
+template <int DIM, typename St>
+constexpr int fold_smem_bytes() {
+  return FoldShape<DIM, St>::SMEM;
+}
+
+// Three resident CTAs per SM; two for 2-byte state tiles, whose 8-wide key
+// slices need more registers.
+template <typename St>
+constexpr int fold_min_blocks() {
+  return sizeof(St) == 4 ? 3 : 2;
+}
+
+template <int DIM, typename St, typename Kt>
+__global__ void __launch_bounds__(kFoldThreads, fold_min_blocks<St>()) fold_kernel(const FoldParams p) {
+  using Sh = FoldShape<DIM, St>;
+  constexpr int EPC = Sh::EPC, CPR = Sh::CPR, RSTEP = Sh::RSTEP, CPT = Sh::CPT;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+  unsigned char *tile = smem;
+  float(*s_corr)[DIM] = reinterpret_cast<float(*)[DIM]>(smem + Sh::TILE);
+  float *s_decay = reinterpret_cast<float *>(smem + Sh::TILE + Sh::CORR);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + Sh::TILE + Sh::CORR + 32);
 
   const int64_t HV = p.heads;
   const int64_t unit = blockIdx.x;
@@ -95,16 +116,32 @@ __global__ void __launch_bounds__(kFoldThreads, 2) fold_kernel(const FoldParams 
   const int64_t bidx = p.boundaries[prow];
   const int blen = p.boundary_lens[prow];
   const bool store_b = bidx > p.null_block && bidx < p.blocks && bidx != fin && blen > 0;
-
-  const bool packed = (p.flags & GDN_RSSM_FOLD_PACKED) != 0;
   St *state = reinterpret_cast<St *>(p.state_addrs[layer]);
   const int64_t sbs = p.state_bs[layer];
-  // 16-byte vector access needs a 16-byte aligned page base (the head / row
-  // strides were checked on the host); refuse the unit instead of faulting.
+  // 16-byte copies and stores need a 16-byte aligned page base (head / row
+  // strides were checked on the host): refuse the unit instead of faulting.
   if ((reinterpret_cast<uintptr_t>(state) & 15) != 0 || sbs % EPC != 0) {
     if (threadIdx.x == 0) atomicExch(p.status, kStatusMisaligned);
     return;
   }
+  const int tid = threadIdx.x;
+  const St *src_tile = state + src * sbs + head * p.state_hs;
+  if (tid < 32) {
+    if (tid == 0) {
+      ptx::mbar_init(bar, 1);
+      ptx::fence_mbar_init();
+      ptx::mbar_arrive_expect_tx(bar, Sh::TILE);
+    }
+    __syncwarp();
+    if (p.state_vs == DIM) {
+      if (tid == 0) ptx::bulk_load(tile, src_tile, Sh::TILE, bar);
+    } else {
+      for (int r = tid; r < DIM; r += 32)
+        ptx::bulk_load(tile + r * DIM * sizeof(St), src_tile + r * p.state_vs, DIM * sizeof(St), bar);
+    }
+  }
+  // window records: corr -> shared, decay -> shared, this thread's key slice -> registers
+  const bool packed = (p.flags & GDN_RSSM_FOLD_PACKED) != 0;
   const float *corr = reinterpret_cast<const float *>(p.corr_addrs[layer]) + row * p.corr_bs[layer] + head * p.corr_hs;
   const Kt *keyp;
   const float *decp;
@@ -121,54 +158,60 @@ __global__ void __launch_bounds__(kFoldThreads, 2) fold_kernel(const FoldParams 
     key_ts = p.key_ts;
     dec_ts = p.decay_ts;
   }
-
-  const int tid = threadIdx.x;
-  const int col = tid % CPR;      // fixed 16-B column chunk of this thread
-  const int rbase = tid / CPR;    // rows rbase, rbase + RSTEP, ...
-  const St *src_tile = state + src * sbs + head * p.state_hs;
-
-  // issue every state load of this thread first
-  uint4 raw[CPT];
+  const int col = tid % CPR;    // fixed 16-byte column chunk of this thread
+  const int rbase = tid / CPR;  // rows rbase, rbase + RSTEP, ...
+  float cv[kMaxWindow * DIM / kFoldThreads + 1];
+  {
+    // issue every record load before any store (one memory round trip)
+    constexpr int PER = (kMaxWindow * DIM + kFoldThreads - 1) / kFoldThreads;
 #pragma unroll
-  for (int i = 0; i < CPT; ++i) {
-    const int r = rbase + i * RSTEP;
-    if (DIM % RSTEP == 0 || r < DIM) raw[i] = __ldcs(reinterpret_cast<const uint4 *>(src_tile + r * p.state_vs + col * EPC));
+    for (int c = 0; c < PER; ++c) {
+      const int idx = tid + c * kFoldThreads;
+      const int t = idx / DIM, e = idx % DIM;
+      cv[c] = (t < n) ? corr[t * p.corr_ts + e] : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < PER; ++c) {
+      const int idx = tid + c * kFoldThreads;
+      const int t = idx / DIM, e = idx % DIM;
+      if (t < n) s_corr[t][e] = cv[c];
+    }
   }
-  // window records: corr -> shared, decay -> shared, key slice -> registers
-  for (int i = tid; i < n * DIM; i += kFoldThreads) {
-    const int t = i / DIM, e = i % DIM;
-    s_corr[t][e] = corr[t * p.corr_ts + e];
-  }
-  if (tid < n) s_decay[tid] = decp[tid * dec_ts];
   float kk[kMaxWindow][EPC];
+  float dd[kMaxWindow];
 #pragma unroll
   for (int t = 0; t < kMaxWindow; ++t) {
+    dd[t] = t < n ? decp[t * dec_ts] : 1.f;
 #pragma unroll
     for (int e = 0; e < EPC; ++e) kk[t][e] = t < n ? to_f32<Kt>(keyp[t * key_ts + col * EPC + e]) : 0.f;
   }
-  __syncthreads();
-
+  (void)s_decay;
+  __syncthreads();  // corr staged; barrier initialised
+  if (!ptx::mbar_wait_bounded(bar, 0, kFoldWaitLimitNs)) {
+    if (tid == 0) atomicExch(p.status, kStatusTmaTimeout);
+    ptx::mbar_wait_bounded(bar, 0, kFoldWaitLimitNs);  // let an in-flight copy land before exiting
+    return;
+  }
   St *fin_tile = state + fin * sbs + head * p.state_hs;
   St *b_tile = state + bidx * sbs + head * p.state_hs;
-#pragma unroll
+#pragma unroll 4
   for (int i = 0; i < CPT; ++i) {
     const int r = rbase + i * RSTEP;
     if (DIM % RSTEP != 0 && r >= DIM) break;
-    float hcur[EPC];
-    unpack16(raw[i], hcur, St());
+    const uint4 raw = *reinterpret_cast<const uint4 *>(tile + (r * DIM + col * EPC) * sizeof(St));
+    float h[EPC];
+    unpack16(raw, h, St());
 #pragma unroll
     for (int t = 0; t < kMaxWindow; ++t) {
       if (t < n) {
         const float c = s_corr[t][r];
-        const float d = s_decay[t];
 #pragma unroll
-        for (int e = 0; e < EPC; ++e) hcur[e] = fmaf(c, kk[t][e], hcur[e] * d);
-        if (store_b && t + 1 == blen) {
-          *reinterpret_cast<uint4 *>(b_tile + r * p.state_vs + col * EPC) = pack16(hcur, St());
-        }
+        for (int e = 0; e < EPC; ++e) h[e] = fmaf(c, kk[t][e], h[e] * dd[t]);
+        if (store_b && t + 1 == blen)
+          *reinterpret_cast<uint4 *>(b_tile + r * p.state_vs + col * EPC) = pack16(h, St());
       }
     }
-    *reinterpret_cast<uint4 *>(fin_tile + r * p.state_vs + col * EPC) = pack16(hcur, St());
+    *reinterpret_cast<uint4 *>(fin_tile + r * p.state_vs + col * EPC) = pack16(h, St());
   }
 }
 

@@ -1,4 +1,4 @@
-// Speculative verify kernel (sm_100a).
+// Speculative verify kernel (sm_100a): persistent, warp-specialised pipeline.
 //
 // Semantics follow the reference verify (kernels.py:491-697; AscendC
 // verify.h:350-398): per (sequence row, value head) "unit", read the fp32
@@ -6,23 +6,30 @@
 // tokens, write the attention output per token and one record per token
 // [corr(V), k_hat(K), decay].
 //
-// B200 design.  One CTA (256 threads) per unit, up to 3 resident per SM.
-//  * The whole S tile is staged into shared memory by TMA (4-D tensor map over
-//    the [blocks, HV, V, K] pool, 128-byte swizzle, boxes of 128 B x V rows),
-//    so each thread can read "its" state row 16 B at a time without bank
-//    conflicts while the tile is in flight for the other resident CTAs.
-//  * The Q-step recurrence is evaluated in its chunked form: with
-//    A_t = prod_{s<=t} d_s and D[t][s] = prod_{s<r<=t} d_r,
-//        S'_t k_t = A_t (S_0 k_t) + sum_{s<t}  D[t][s] (k_s . k_t) c_s
-//        S_t q_t  = A_t (S_0 q_t) + sum_{s<=t} D[t][s] (k_s . q_t) c_s
-//        c_t      = beta_t (v_t - S'_t k_t)
-//    so the only O(V K) work is ONE pass over S_0 computing 2Q dot products
-//    per row (S_0 [k_1..k_Q, q_1..q_Q]); the per-token recurrence is O(Q^2)
-//    scalar work per row.  No rank-1 update of the tile is ever materialised
-//    and nothing is serialised behind a cross-lane reduction per token.
-//  * Rows map to lanes (RPW rows per warp), the K extent is split KSPLIT ways
-//    across lane groups and reduced with warp shuffles; the 2Q key/query
-//    vectors live in shared memory and are read as warp-uniform broadcasts.
+// Math.  The Q-step recurrence is evaluated in its chunked form.  With
+// A_t = prod_{s<=t} d_s and D[t][s] = prod_{s<r<=t} d_r,
+//     S'_t k_t = A_t (S_0 k_t) + sum_{s<t}  D[t][s] (k_s . k_t) c_s
+//     S_t q_t  = A_t (S_0 q_t) + sum_{s<=t} D[t][s] (k_s . q_t) c_s
+//     c_t      = beta_t (v_t - S'_t k_t),      o_t = S_t q_t
+// so the only O(V K) work is one pass over S_0 computing 2Q dot products per
+// state row; the per-token recurrence is O(Q^2) scalar work per row.
+//
+// B200 design: one CTA (256 threads, 8 warps) per unit, two or three resident
+// per SM so that several 64 KiB tiles are in flight per SM.
+//  * Thread 0 starts the TMA tile load of S_0 first (4-D tensor map over the
+//    [blocks, HV, V, K] pool, 128-byte swizzle, one box per 128 bytes of K).
+//  * While it flies, the warps stage the window: q/k/v/g/beta are loaded in
+//    one memory round trip, q/k optionally L2-normalised, written to shared
+//    memory as fp32 X rows (k_hat then q_tilde, in the tile's chunk order), the
+//    key/decay records are written, and the Gram dot products k_s.k_t,
+//    k_s.q_t plus the decay coefficients are computed (one pair per warp).
+//  * One register-blocked pass over the swizzled tile: each thread owns
+//    R = K/32 rows and 1/8 of K; the 8 K-groups of a quarter warp read one
+//    contiguous 128-byte segment of the tile and of X (no bank conflicts) and
+//    each X chunk feeds R rows.  A lane-group reduce-scatter gathers each row's
+//    2Q sums, then the per-row recurrence writes the output and correction.
+// Two CTA barriers in all, both before the tile is needed; the tile wait is
+// bounded.
 //
 // Invalid tokens (t >= qlen or token index out of range) contribute decay 1,
 // beta 0 and zero q/k: they change nothing and store nothing, exactly like the
@@ -55,40 +62,37 @@ struct VerifyParams {
   uint32_t flags;
 };
 
-template <int DIM, int QT, typename St>
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+
+template <int DIM, int QT, typename Act, typename St>
 struct VerifyShape {
-  static constexpr int kThreads = kVerifyThreads;
-  static constexpr int KSPLIT = kThreads / DIM;         // lane groups splitting K
-  static constexpr int RPW = 32 / KSPLIT;               // rows per warp
-  static constexpr int KC = DIM / KSPLIT;               // K elements per lane group
-  static constexpr int EPC = 16 / sizeof(St);           // state elements per 16-B chunk
-  static constexpr int BOXW = 128 / sizeof(St);         // state elements per swizzled box row
-  static constexpr int NBOX = DIM / BOXW;               // boxes per tile
-  static constexpr int LDX = DIM + 4 * KSPLIT;          // padded X row (floats)
-  static constexpr int TILE_BYTES = DIM * DIM * sizeof(St);
-  static constexpr int X_BYTES = 2 * QT * LDX * 4;
-  static constexpr int NPAIR = QT * QT;                 // Gram pairs (k.k s<t, k.q s<=t)
+  static constexpr int NJ = 2 * QT;              // dot products per state row
+  static constexpr int EPC = 16 / sizeof(St);    // state elements per 16-byte chunk
+  static constexpr int BOXW = 128 / sizeof(St);  // state elements per swizzled box row
+  static constexpr int NBOX = DIM / BOXW;        // boxes (= chunks per K-group) per row
+  static constexpr int R = DIM / 32;             // rows per consumer thread
+  static constexpr int EPL = DIM / 32;           // K elements per prep lane
+  static constexpr int NP = QT * QT;             // Gram pairs (k.k s<t, then k.q s<=t)
+  static constexpr int V = R * NJ;               // partial sums per consumer thread
+  static constexpr int TILE = DIM * DIM * sizeof(St);
+  struct Small {
+    uint64_t bar;
+    float A[QT];
+    float beta[QT];
+    float dec[QT];
+    float mkk[QT][QT];  // D[t][s] * (k_s . k_t), s < t
+    float mkq[QT][QT];  // D[t][s] * (k_s . q_t), s <= t
+  };
+  static constexpr int X_BYTES = NJ * DIM * 4;
+  static constexpr int V_BYTES = (QT * DIM * static_cast<int>(sizeof(Act)) + 15) / 16 * 16;
+  static constexpr int SMEM = 1024 /* alignment slack */ + TILE + X_BYTES + V_BYTES + static_cast<int>(sizeof(Small));
   static_assert(DIM % BOXW == 0, "state tile must be whole swizzle boxes");
-  static_assert(KC % EPC == 0, "lane group K range must be whole chunks");
-  static_assert(KSPLIT * RPW == 32, "lane layout");
+  static_assert(R >= 1 && R <= 4, "rows per thread");
 };
 
-template <int QT>
-struct VerifySmall {
-  uint64_t bar;
-  float dec[QT];    // decay of token t (1 for invalid tokens)
-  float beta[QT];   // beta of token t (0 for invalid tokens)
-  float A[QT];      // prod_{s<=t} dec[s]
-  float mkk[QT][QT];  // D[t][s] * (k_s . k_t), s < t
-  float mkq[QT][QT];  // D[t][s] * (k_s . q_t), s <= t
-  int32_t valid[QT];
-  int32_t tok[QT];
-};
-
-template <int DIM, int QT, typename St>
+template <int DIM, int QT, typename Act, typename St>
 constexpr int verify_smem_bytes() {
-  using Sh = VerifyShape<DIM, QT, St>;
-  return 1024 /* alignment slack */ + Sh::TILE_BYTES + Sh::X_BYTES + static_cast<int>(sizeof(VerifySmall<QT>));
+  return VerifyShape<DIM, QT, Act, St>::SMEM;
 }
 
 __device__ __forceinline__ int64_t load_typed_index(const void *p, int64_t i, int32_t dtype) {
@@ -104,8 +108,43 @@ __device__ __forceinline__ void store_key(void *p, int64_t i, float x, int32_t d
   }
 }
 
-// Three CTAs per SM keep ~3 state tiles in flight; the Q = 8 variant trades one
-// resident CTA for registers (its 2Q accumulators would otherwise spill).
+// Position of K element e inside an X row: the tile's 16-byte chunk order, so
+// that the 8 K-groups of a quarter warp read 128 contiguous bytes of X.
+// (Identity for fp32 tiles.)
+template <int BOXW, int EPC>
+__device__ __forceinline__ int x_pos(int e) {
+  const int m = e / BOXW, kg = (e % BOXW) / EPC, w = e % EPC;
+  return m * BOXW + (w / 4) * 32 + kg * 4 + (w % 4);
+}
+
+// Sums NV per-lane values over the lanes that differ in the bits HI, HI/2,
+// ..., 1 of the lane index.  While more than one value is left, a level keeps
+// half of them (lanes with the bit set keep the upper half) and adds the
+// partner's copy; once one value is left the remaining levels all-reduce it.
+// With NV >= 2^levels, the lane whose selected bits read b holds the sums of
+// indices [b * NV / 2^levels, (b + 1) * NV / 2^levels).
+template <int NV, int HI>
+__device__ __forceinline__ void reduce_scatter(float *a, int lane) {
+  if constexpr (HI >= 1) {
+    if constexpr (NV >= 2) {
+      constexpr int half = NV / 2;
+      const bool upper = (lane & HI) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? a[i] : a[i + half];
+        const float keep = upper ? a[i + half] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, HI);
+      }
+      reduce_scatter<half, HI / 2>(a, lane);
+    } else {
+      a[0] += __shfl_xor_sync(0xffffffffu, a[0], HI);
+      reduce_scatter<1, HI / 2>(a, lane);
+    }
+  }
+}
+
+// Resident CTAs per SM: three while the window is short, two at Q = 8 (its 2Q
+// accumulators per row need the registers and the larger X the shared memory).
 template <int QT>
 constexpr int verify_min_blocks() {
   return QT >= 8 ? 2 : 3;
@@ -114,13 +153,16 @@ constexpr int verify_min_blocks() {
 template <int DIM, int QT, typename Act, typename St>
 __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
     verify_kernel(const __grid_constant__ CUtensorMap state_map, const VerifyParams p) {
-  using Sh = VerifyShape<DIM, QT, St>;
+  using Sh = VerifyShape<DIM, QT, Act, St>;
+  using Small = typename Sh::Small;
+  constexpr int NJ = Sh::NJ, EPC = Sh::EPC, BOXW = Sh::BOXW, R = Sh::R, EPL = Sh::EPL, V = Sh::V;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char *tile = smem;
-  float *X = reinterpret_cast<float *>(smem + Sh::TILE_BYTES);
-  VerifySmall<QT> &sm = *reinterpret_cast<VerifySmall<QT> *>(smem + Sh::TILE_BYTES + Sh::X_BYTES);
+  float(*X)[DIM] = reinterpret_cast<float(*)[DIM]>(smem + Sh::TILE);
+  Act(*vs)[DIM] = reinterpret_cast<Act(*)[DIM]>(smem + Sh::TILE + Sh::X_BYTES);
+  Small &sm = *reinterpret_cast<Small *>(smem + Sh::TILE + Sh::X_BYTES + Sh::V_BYTES);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -129,227 +171,268 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
   const int hv = static_cast<int>(blockIdx.x % HV);
   const int ratio = static_cast<int>(HV / p.heads);
   const int h = hv / ratio;
+  const int Q = static_cast<int>(p.query_len);
 
   const int64_t bos = load_typed_index(p.qsl, row * p.qsl_stride, p.qsl_dtype);
   const int64_t eos = load_typed_index(p.qsl, (row + 1) * p.qsl_stride, p.qsl_dtype);
   const int64_t qlen = eos - bos;
   const int64_t slot = load_typed_index(p.indices, row * p.index_stride, p.index_dtype);
-  const int Q = static_cast<int>(p.query_len);
+  int valid_mask = 0;
+#pragma unroll
+  for (int t = 0; t < QT; ++t) {
+    const int64_t tok = bos + t;
+    if (t < Q && t < qlen && tok >= 0 && tok < p.tokens) valid_mask |= 1 << t;
+  }
+  Act *out = static_cast<Act *>(p.out);
 
   // ---- null / out-of-pool slot: zero output for the row's window ---------- //
   if (slot <= p.null_block || slot >= p.blocks) {
-    Act *out = static_cast<Act *>(p.out);
     for (int i = tid; i < QT * DIM; i += kVerifyThreads) {
       const int t = i / DIM, e = i % DIM;
-      const int64_t tok = bos + t;
-      if (t < Q && t < qlen && tok >= 0 && tok < p.tokens) out[tok * p.out_ts + hv * DIM + e] = from_f32<Act>(0.f);
+      if ((valid_mask >> t) & 1) out[(bos + t) * p.out_ts + hv * DIM + e] = from_f32<Act>(0.f);
     }
     return;
   }
 
-  // ---- issue the TMA tile load first so it overlaps all the set-up -------- //
+  // ---- start the tile load first so it overlaps all of the set-up --------- //
   if (tid == 0) {
     ptx::prefetch_tensormap(&state_map);
     ptx::mbar_init(&sm.bar, 1);
     ptx::fence_mbar_init();
-    ptx::mbar_arrive_expect_tx(&sm.bar, Sh::TILE_BYTES);
+    ptx::mbar_arrive_expect_tx(&sm.bar, Sh::TILE);
 #pragma unroll
-    for (int b = 0; b < Sh::NBOX; ++b) {
-      ptx::tma_load_4d(tile + b * DIM * 128, &state_map, &sm.bar, b * Sh::BOXW, 0, hv, static_cast<int32_t>(slot));
+    for (int m = 0; m < Sh::NBOX; ++m) {
+      ptx::tma_load_4d(tile + m * DIM * 128, &state_map, &sm.bar, m * BOXW, 0, hv, static_cast<int32_t>(slot));
     }
   }
-  // ---- per-token scalars ---------------------------------------------------- //
-  if (tid < QT) {
-    const int t = tid;
-    const int64_t tok = bos + t;
-    const bool valid = t < Q && t < qlen && tok >= 0 && tok < p.tokens;
-    sm.valid[t] = valid;
-    sm.tok[t] = valid ? static_cast<int32_t>(tok) : 0;
-    sm.dec[t] = valid ? expf(p.g[tok * p.g_ts + hv]) : 1.f;
-    sm.beta[t] = valid ? load_float(p.beta, tok * p.beta_ts + hv, p.beta_dtype) : 0.f;
-  }
-  __syncthreads();
 
-  // ---- stage k_hat and q_tilde (fp32) into X, optional in-kernel L2 ------- //
+  // ---- stage the window ------------------------------------------------------ //
   const bool normalize = (p.flags & GDN_RSSM_NORMALIZE_QK) != 0;
-  for (int j = warp; j < 2 * QT; j += kVerifyThreads / 32) {
-    const int t = j % QT;
-    const bool is_q = j >= QT;
-    float x[DIM / 32];
-    const bool valid = sm.valid[t];
-    const Act *src = static_cast<const Act *>(is_q ? p.q : p.k);
-    const int64_t base = static_cast<int64_t>(sm.tok[t]) * (is_q ? p.q_ts : p.k_ts) + static_cast<int64_t>(h) * DIM;
-    float ss = 0.f;
+  const bool packed = (p.flags & GDN_RSSM_RECORD_PACKED) != 0;
+  const bool rec_ok = row < p.record_rows;
+  {
+    // q/k rows: warp w owns vectors w, w + 8, ... (k_t for j < QT, q_t after)
+    constexpr int PER_WARP = (NJ + 7) / 8;
+    float x[PER_WARP][EPL];
 #pragma unroll
-    for (int i = 0; i < DIM / 32; ++i) {
-      x[i] = valid ? to_f32<Act>(src[base + lane + 32 * i]) : 0.f;
-      ss = fmaf(x[i], x[i], ss);
+    for (int c = 0; c < PER_WARP; ++c) {
+      const int j = warp + 8 * c;
+      const int t = j % QT;
+      const bool live = j < NJ && ((valid_mask >> t) & 1);
+      const Act *src = static_cast<const Act *>(j >= QT ? p.q : p.k);
+      const int64_t base = (bos + t) * (j >= QT ? p.q_ts : p.k_ts) + static_cast<int64_t>(h) * DIM + lane * EPL;
+#pragma unroll
+      for (int u = 0; u < EPL; ++u) x[c][u] = live ? to_f32<Act>(src[base + u]) : 0.f;
     }
-    float mul = 1.f;
-    if (normalize) {
+    // v rows (raw activation values) and per-token scalars
+    const Act *vin = static_cast<const Act *>(p.v);
+    constexpr int VPER = (QT * DIM + kVerifyThreads - 1) / kVerifyThreads;
+    Act vv[VPER];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      mul = rsqrtf(ss + 1e-6f);
+    for (int c = 0; c < VPER; ++c) {
+      const int i = tid + c * kVerifyThreads;
+      const int t = i / DIM, e = i % DIM;
+      vv[c] = (i < QT * DIM && ((valid_mask >> t) & 1)) ? vin[(bos + t) * p.v_ts + hv * DIM + e] : from_f32<Act>(0.f);
+    }
+    float dec = 1.f, bet = 0.f;
+    if (tid < QT && ((valid_mask >> tid) & 1)) {
+      dec = expf(p.g[(bos + tid) * p.g_ts + hv]);
+      bet = load_float(p.beta, (bos + tid) * p.beta_ts + hv, p.beta_dtype);
     }
 #pragma unroll
-    for (int i = 0; i < DIM / 32; ++i) {
-      const int e = lane + 32 * i;
-      float val = normalize ? x[i] * mul : x[i];
-      if (is_q) val *= p.scale;
-      X[j * Sh::LDX + (e / Sh::KC) * (Sh::KC + 4) + (e % Sh::KC)] = val;
+    for (int c = 0; c < VPER; ++c) {
+      const int i = tid + c * kVerifyThreads;
+      if (i < QT * DIM) vs[i / DIM][i % DIM] = vv[c];
+    }
+    if (tid < QT) {
+      sm.dec[tid] = dec;
+      sm.beta[tid] = bet;
+      if (rec_ok && ((valid_mask >> tid) & 1)) p.decay[row * p.decay_rs + hv * p.decay_hs + tid * p.decay_ts] = dec;
+    }
+#pragma unroll
+    for (int c = 0; c < PER_WARP; ++c) {
+      const int j = warp + 8 * c;
+      if (j >= NJ) continue;
+      const int t = j % QT;
+      if (normalize) {
+        float ss = 0.f;
+#pragma unroll
+        for (int u = 0; u < EPL; ++u) ss = fmaf(x[c][u], x[c][u], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float mul = rsqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int u = 0; u < EPL; ++u) x[c][u] *= mul;
+      }
+      if (j < QT) {
+        // key record: packed -> every value head keeps its copy; typed -> once per key head
+        if (rec_ok && ((valid_mask >> t) & 1) && (packed || hv % ratio == 0)) {
+          const int64_t kh = packed ? hv : h;
+          const int32_t kd = packed ? GDN_RSSM_F32 : p.key_dtype;
+#pragma unroll
+          for (int u = 0; u < EPL; ++u)
+            store_key(p.key, row * p.key_rs + kh * p.key_hs + t * p.key_ts + lane * EPL + u, x[c][u], kd);
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < EPL; ++u) x[c][u] *= p.scale;
+      }
+#pragma unroll
+      for (int u = 0; u < EPL; ++u) X[j][x_pos<BOXW, EPC>(lane * EPL + u)] = x[c][u];
     }
   }
-  __syncthreads();
+  __syncthreads();  // X, v, dec, beta staged; barrier initialised
 
   // ---- Gram coefficients: one pair per warp iteration ---------------------- //
-  for (int pr = warp; pr < Sh::NPAIR; pr += kVerifyThreads / 32) {
-    // pairs [0, QT(QT-1)/2): k_s.k_t (s<t); then QT(QT+1)/2 pairs k_s.q_t (s<=t)
-    int s, t, kind;
-    {
-      int idx = pr;
-      kind = 0;
-      const int nkk = QT * (QT - 1) / 2;
-      if (idx >= nkk) {
-        kind = 1;
-        idx -= nkk;
-      }
-      // decode lower-triangular index
-      t = 0;
-      int lim = kind == 0 ? 0 : 1;  // number of s for t=0
-      while (idx >= lim + t) {
-        idx -= lim + t;
+  {
+    constexpr int NKK = QT * (QT - 1) / 2;
+    for (int pr = warp; pr < Sh::NP; pr += 8) {
+      const int kind = pr >= NKK ? 1 : 0;
+      int rem = kind ? pr - NKK : pr, t = 0;
+      while (rem >= (kind ? t + 1 : t)) {
+        rem -= kind ? t + 1 : t;
         ++t;
       }
-      s = idx;
-    }
-    const float *a = X + s * Sh::LDX;
-    const float *b = X + (kind == 0 ? t : QT + t) * Sh::LDX;
-    float acc = 0.f;
+      const int s2 = rem;
+      const float *a = X[s2];
+      const float *b = X[kind ? QT + t : t];
+      float acc = 0.f;
 #pragma unroll
-    for (int i = 0; i < DIM / 32; ++i) {
-      const int e = lane + 32 * i;
-      const int xi = (e / Sh::KC) * (Sh::KC + 4) + (e % Sh::KC);
-      acc = fmaf(a[xi], b[xi], acc);
-    }
+      for (int u = 0; u < EPL; ++u) acc = fmaf(a[lane + 32 * u], b[lane + 32 * u], acc);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) {
-      float dprod = 1.f;
-      for (int r = s + 1; r <= t; ++r) dprod *= sm.dec[r];
-      if (kind == 0) {
-        sm.mkk[t][s] = dprod * acc;
-      } else {
-        sm.mkq[t][s] = dprod * acc;
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        float d = 1.f;
+        for (int r2 = s2 + 1; r2 <= t; ++r2) d *= sm.dec[r2];
+        if (kind == 0) {
+          sm.mkk[t][s2] = d * acc;
+        } else {
+          sm.mkq[t][s2] = d * acc;
+        }
+      }
+    }
+    if (tid == 0) {
+      float a = 1.f;
+#pragma unroll
+      for (int t = 0; t < QT; ++t) {
+        a *= sm.dec[t];
+        sm.A[t] = a;
       }
     }
   }
-  if (tid == 0) {
-    float a = 1.f;
-#pragma unroll
-    for (int t = 0; t < QT; ++t) {
-      a *= sm.dec[t];
-      sm.A[t] = a;
-    }
-  }
-
-  // ---- records: key and decay (independent of the state) ------------------ //
-  const bool rec_ok = row < p.record_rows;
-  const bool packed = (p.flags & GDN_RSSM_RECORD_PACKED) != 0;
-  if (rec_ok) {
-    if (tid < QT && sm.valid[tid]) {
-      p.decay[row * p.decay_rs + hv * p.decay_hs + tid * p.decay_ts] = sm.dec[tid];
-    }
-    if (packed || hv % ratio == 0) {
-      const int64_t kh = packed ? hv : h;
-      for (int i = tid; i < QT * DIM; i += kVerifyThreads) {
-        const int t = i / DIM, e = i % DIM;
-        if (!sm.valid[t]) continue;
-        const float val = X[t * Sh::LDX + (e / Sh::KC) * (Sh::KC + 4) + (e % Sh::KC)];
-        store_key(p.key, row * p.key_rs + kh * p.key_hs + t * p.key_ts + e, val, packed ? GDN_RSSM_F32 : p.key_dtype);
-      }
-    }
-  }
-
-  // ---- row ownership: r = warp*RPW + lane%RPW, K split ks = lane/RPW ------- //
-  const int r = warp * Sh::RPW + (lane % Sh::RPW);
-  const int ks = lane / Sh::RPW;
-  __syncthreads();  // Gram coefficients visible
+  __syncthreads();  // coefficients visible
 
   // ---- wait for the tile ----------------------------------------------------- //
-  if (!ptx::mbar_wait_bounded(&sm.bar, 0, 1000000000ull)) {
+  if (!ptx::mbar_wait_bounded(&sm.bar, 0, kWaitLimitNs)) {
     if (tid == 0) atomicExch(p.status, kStatusTmaTimeout);
-    ptx::mbar_wait_bounded(&sm.bar, 0, 1000000000ull);  // let an in-flight copy land before exiting
+    ptx::mbar_wait_bounded(&sm.bar, 0, kWaitLimitNs);  // let an in-flight copy land before exiting
     return;
   }
 
-  // ---- one pass over S_0: acc[j] = sum_k S[r][k] X[j][k] over this lane's K range //
-  float acc[2 * QT];
+  // ---- one pass over S_0: thread = R rows x 1/8 of K --------------------------- //
+  const int kg = lane & 7;                  // K-group: chunk kg of every box
+  const int r0 = (warp * 4 + (lane >> 3)) * R;  // first row of this thread
+  float acc[V];
 #pragma unroll
-  for (int j = 0; j < 2 * QT; ++j) acc[j] = 0.f;
-  const unsigned char *trow = tile + r * 128;
-  const float *xk = X + ks * (Sh::KC + 4);
-#pragma unroll 4
-  for (int cc = 0; cc < Sh::KC / Sh::EPC; ++cc) {
-    const int k0 = ks * Sh::KC + cc * Sh::EPC;  // first element of this chunk
-    const int box = k0 / Sh::BOXW;
-    const int c = (k0 % Sh::BOXW) / Sh::EPC;
-    const uint4 raw = *reinterpret_cast<const uint4 *>(trow + box * DIM * 128 + ((c ^ (r & 7)) << 4));
-    float s[Sh::EPC];
-    if constexpr (sizeof(St) == 4) {
-      s[0] = __uint_as_float(raw.x);
-      s[1] = __uint_as_float(raw.y);
-      s[2] = __uint_as_float(raw.z);
-      s[3] = __uint_as_float(raw.w);
-    } else {
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  for (int a = 0; a < V; ++a) acc[a] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        s[2 * i] = __uint_as_float(w[i] << 16);
-        s[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  for (int m = 0; m < Sh::NBOX; ++m) {
+    float sv[R][EPC];
+#pragma unroll
+    for (int a = 0; a < R; ++a) {
+      const int r = r0 + a;
+      const uint4 raw = *reinterpret_cast<const uint4 *>(tile + m * DIM * 128 + r * 128 + ((kg ^ (r & 7)) << 4));
+      if constexpr (sizeof(St) == 4) {
+        sv[a][0] = __uint_as_float(raw.x);
+        sv[a][1] = __uint_as_float(raw.y);
+        sv[a][2] = __uint_as_float(raw.z);
+        sv[a][3] = __uint_as_float(raw.w);
+      } else {
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          sv[a][2 * u] = __uint_as_float(w4[u] << 16);
+          sv[a][2 * u + 1] = __uint_as_float(w4[u] & 0xffff0000u);
+        }
       }
     }
-    const float *xc = xk + cc * Sh::EPC;
 #pragma unroll
-    for (int j = 0; j < 2 * QT; ++j) {
+    for (int j = 0; j < NJ; ++j) {
 #pragma unroll
-      for (int e4 = 0; e4 < Sh::EPC; e4 += 4) {
-        const float4 x4 = *reinterpret_cast<const float4 *>(xc + j * Sh::LDX + e4);
-        acc[j] = fmaf(s[e4 + 0], x4.x, acc[j]);
-        acc[j] = fmaf(s[e4 + 1], x4.y, acc[j]);
-        acc[j] = fmaf(s[e4 + 2], x4.z, acc[j]);
-        acc[j] = fmaf(s[e4 + 3], x4.w, acc[j]);
+      for (int e4 = 0; e4 < EPC / 4; ++e4) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(&X[j][m * BOXW + e4 * 32 + kg * 4]);
+#pragma unroll
+        for (int a = 0; a < R; ++a) {
+          float &ac = acc[a * NJ + j];
+          ac = fmaf(sv[a][e4 * 4 + 0], x4.x, ac);
+          ac = fmaf(sv[a][e4 * 4 + 1], x4.y, ac);
+          ac = fmaf(sv[a][e4 * 4 + 2], x4.z, ac);
+          ac = fmaf(sv[a][e4 * 4 + 3], x4.w, ac);
+        }
       }
     }
   }
-  // reduce the KSPLIT partial sums (lanes l, l^RPW, l^2RPW, ...)
+  // ---- reduce the 8 K-groups and gather each row's 2Q sums ----------------- //
+  constexpr bool SCATTER = V >= 8;              // else a plain all-reduce
+  constexpr int C = SCATTER ? V / 8 : V;        // values held after the scatter
+  constexpr int LPR = SCATTER ? NJ / C : 1;     // lanes sharing one row (= 8 / R)
+  float pr[NJ];
+  int my_row;
+  bool writer_out, writer_corr;
+  if constexpr (SCATTER) {
+    reduce_scatter<V, 4>(acc, lane);
+    // lane kg now holds flat indices [kg*C, kg*C + C): row kg*C/NJ, j from (kg*C)%NJ
+    my_row = (kg * C) / NJ;
+    const int jbase = (kg * C) % NJ;
 #pragma unroll
-  for (int o = Sh::RPW; o < 32; o <<= 1) {
+    for (int j = 0; j < NJ; ++j) {
+      float v = 0.f;
 #pragma unroll
-    for (int j = 0; j < 2 * QT; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+      for (int c = 0; c < C; ++c)
+        if (j == jbase + c) v = acc[c];
+      pr[j] = v;
+    }
+#pragma unroll
+    for (int o = 1; o < LPR; o <<= 1) {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) pr[j] += __shfl_xor_sync(0xffffffffu, pr[j], o);
+    }
+    writer_out = (kg % LPR) == LPR - 1;
+    writer_corr = (kg % LPR) == 0;
+  } else {
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+#pragma unroll
+      for (int a = 0; a < V; ++a) acc[a] += __shfl_xor_sync(0xffffffffu, acc[a], o);
+    }
+    my_row = kg < R ? kg : 0;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      float v = 0.f;
+#pragma unroll
+      for (int a = 0; a < R; ++a)
+        if (a == my_row) v = acc[a * NJ + j];
+      pr[j] = v;
+    }
+    writer_out = writer_corr = kg < R;
   }
-  if (ks != 0) return;
-
-  // ---- per-row recurrence over the window ---------------------------------- //
-  Act *out = static_cast<Act *>(p.out);
-  const Act *vin = static_cast<const Act *>(p.v);
-  float vv[QT];
-#pragma unroll
-  for (int t = 0; t < QT; ++t) vv[t] = sm.valid[t] ? to_f32<Act>(vin[static_cast<int64_t>(sm.tok[t]) * p.v_ts + hv * DIM + r]) : 0.f;
+  // ---- per-row recurrence over the window ------------------------------------ //
+  const int r = r0 + my_row;
   float cr[QT];
 #pragma unroll
   for (int t = 0; t < QT; ++t) {
     cr[t] = 0.f;
-    if (!sm.valid[t]) continue;
-    float kv = sm.A[t] * acc[t];
+    if (!((valid_mask >> t) & 1)) continue;
+    float kv = sm.A[t] * pr[t];
 #pragma unroll
-    for (int s = 0; s < t; ++s) kv = fmaf(sm.mkk[t][s], cr[s], kv);
-    cr[t] = sm.beta[t] * (vv[t] - kv);
-    float o = sm.A[t] * acc[QT + t];
+    for (int s2 = 0; s2 < t; ++s2) kv = fmaf(sm.mkk[t][s2], cr[s2], kv);
+    cr[t] = sm.beta[t] * (to_f32<Act>(vs[t][r]) - kv);
+    float o = sm.A[t] * pr[QT + t];
 #pragma unroll
-    for (int s = 0; s <= t; ++s) o = fmaf(sm.mkq[t][s], cr[s], o);
-    const int64_t tok = sm.tok[t];
-    out[tok * p.out_ts + hv * DIM + r] = from_f32<Act>(o);
-    if (rec_ok) p.corr[row * p.corr_rs + hv * p.corr_hs + t * p.corr_ts + r] = cr[t];
+    for (int s2 = 0; s2 <= t; ++s2) o = fmaf(sm.mkq[t][s2], cr[s2], o);
+    const int64_t tok = bos + t;
+    if (writer_out) out[tok * p.out_ts + hv * DIM + r] = from_f32<Act>(o);
+    if (writer_corr && rec_ok) p.corr[row * p.corr_rs + hv * p.corr_hs + t * p.corr_ts + r] = cr[t];
   }
 }
 

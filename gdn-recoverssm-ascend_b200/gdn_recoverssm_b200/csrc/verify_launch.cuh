@@ -28,7 +28,7 @@ int launch_verify_variant(VerifyLaunch &L) {
   int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, L.p.value_heads, L.p.blocks, L.state_bs, L.state_hs,
                             L.state_vs);
   if (rc != GDN_RSSM_OK) return rc;
-  constexpr int smem = verify_smem_bytes<DIM, QT, St>();
+  constexpr int smem = verify_smem_bytes<DIM, QT, Act, St>();
   static bool configured[64] = {false};
   int dev = 0;
   GDN_CUDA(cudaGetDevice(&dev));
@@ -40,6 +40,7 @@ int launch_verify_variant(VerifyLaunch &L) {
     GDN_CUDA(cudaFuncSetAttribute(verify_kernel<DIM, QT, Act, St>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev] = true;
   }
+  // one CTA per (row, value head) unit
   const int64_t grid = L.p.rows * L.p.value_heads;
   verify_kernel<DIM, QT, Act, St><<<static_cast<unsigned>(grid), kVerifyThreads, smem, L.stream>>>(map, L.p);
   GDN_CUDA(cudaGetLastError());

@@ -93,9 +93,20 @@ def _accepted(spec, gen):
     return a.clamp(1, Q).to(torch.int32)
 
 
-def metadata(cfg: int, seed: int = 0):
+def spec_of(cfg: int, rows: int | None = None, pool: int | None = None) -> dict:
+    """The configuration's shape, optionally with fewer rows / a smaller pool
+    (reduced cases for profiling; the benchmark uses the full shapes)."""
+    spec = dict(CONFIGS[cfg])
+    if rows is not None:
+        spec["B"] = int(rows)
+    if pool is not None:
+        spec["pool"] = int(pool)
+    return spec
+
+
+def metadata(cfg: int, seed: int = 0, rows: int | None = None, pool: int | None = None):
     """Host-side (CPU) metadata of a configuration; identical on every rank."""
-    spec = CONFIGS[cfg]
+    spec = spec_of(cfg, rows, pool)
     gen = torch.Generator().manual_seed(1000 + seed * 17 + cfg)
     B, Q, pool = spec["B"], spec["Q"], spec["pool"]
     accepted = _accepted(spec, gen)
@@ -137,16 +148,17 @@ def metadata(cfg: int, seed: int = 0):
     return meta
 
 
-def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv_dim: int = 0) -> Workload:
+def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv_dim: int = 0,
+         rows: int | None = None, pool: int | None = None) -> Workload:
     """Allocate and fill one configuration's tensors on ``device`` (this
     rank's head shard)."""
-    spec = CONFIGS[cfg]
+    spec = spec_of(cfg, rows, pool)
     B, H, HV, D, Q, pool = spec["B"], spec["H"], spec["HV"], spec["D"], spec["Q"], spec["pool"]
     if H % world or HV % world:
         raise ValueError(f"config {cfg}: {H} key / {HV} value heads do not shard over {world} ranks")
     H, HV = H // world, HV // world
     act = spec["act"]
-    meta = metadata(cfg, seed)
+    meta = metadata(cfg, seed, rows, pool)
     dev = torch.device(device)
     gen = torch.Generator(device=dev).manual_seed(7919 * (seed + 1) + 104729 * rank + cfg)
     T = B * Q
