@@ -71,7 +71,9 @@ int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, in
                               static_cast<cuuint64_t>(value_heads), static_cast<cuuint64_t>(blocks)};
   const cuuint64_t gstride[3] = {static_cast<cuuint64_t>(state_vs * es), static_cast<cuuint64_t>(state_hs * es),
                                  static_cast<cuuint64_t>(state_bs * es)};
-  const cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(dim), 1, 1};
+  // one box = 128 bytes of K x 32 rows (the verify kernel loads the tile in
+  // 32-row quarters, each on its own mbarrier)
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), 32u, 1, 1};
   const cuuint32_t estride[4] = {1, 1, 1, 1};
   const CUresult r = fn(map,
                         state_dtype == GDN_RSSM_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,

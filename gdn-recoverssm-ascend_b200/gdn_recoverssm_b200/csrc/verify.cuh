@@ -64,6 +64,11 @@ struct VerifyParams {
 
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
+// Matvec form: 1 = packed f32x2 FMAs over (even, odd) K pairs, 0 = scalar FMAs.
+#ifndef GDN_RSSM_VERIFY_PACKED_FMA
+#define GDN_RSSM_VERIFY_PACKED_FMA 0
+#endif
+
 template <int DIM, int QT, typename Act, typename St>
 struct VerifyShape {
   static constexpr int NJ = 2 * QT;              // dot products per state row
@@ -75,8 +80,9 @@ struct VerifyShape {
   static constexpr int NP = QT * QT;             // Gram pairs (k.k s<t, then k.q s<=t)
   static constexpr int V = R * NJ;               // partial sums per consumer thread
   static constexpr int TILE = DIM * DIM * sizeof(St);
+  static constexpr int NQ = DIM / 32;          // 32-row quarters of the tile, one mbarrier each
   struct Small {
-    uint64_t bar;
+    uint64_t bar[NQ];
     float A[QT];
     float beta[QT];
     float dec[QT];
@@ -109,12 +115,25 @@ __device__ __forceinline__ void store_key(void *p, int64_t i, float x, int32_t d
 }
 
 // Position of K element e inside an X row: the tile's 16-byte chunk order, so
-// that the 8 K-groups of a quarter warp read 128 contiguous bytes of X.
-// (Identity for fp32 tiles.)
+// that the 8 K-groups of a quarter warp read 128 contiguous bytes of X
+// (identity for fp32 tiles).
 template <int BOXW, int EPC>
 __device__ __forceinline__ int x_pos(int e) {
   const int m = e / BOXW, kg = (e % BOXW) / EPC, w = e % EPC;
   return m * BOXW + (w / 4) * 32 + kg * 4 + (w % 4);
+}
+
+// Packed pair FMA (fma.rn.f32x2, sm_100): acc.lo += s.lo * x.lo and
+// acc.hi += s.hi * x.hi, each rounded like fmaf.
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long s, unsigned long long x,
+                                                    unsigned long long acc) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(s), "l"(x), "l"(acc));
+  return d;
+}
+
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
 }
 
 // Sums NV per-lane values over the lanes that differ in the bits HI, HI/2,
@@ -147,7 +166,7 @@ __device__ __forceinline__ void reduce_scatter(float *a, int lane) {
 // accumulators per row need the registers and the larger X the shared memory).
 template <int QT>
 constexpr int verify_min_blocks() {
-  return QT >= 8 ? 2 : 3;
+  return (QT >= 8 || GDN_RSSM_VERIFY_PACKED_FMA) ? 2 : 3;
 }
 
 template <int DIM, int QT, typename Act, typename St>
@@ -197,12 +216,18 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
   // ---- start the tile load first so it overlaps all of the set-up --------- //
   if (tid == 0) {
     ptx::prefetch_tensormap(&state_map);
-    ptx::mbar_init(&sm.bar, 1);
-    ptx::fence_mbar_init();
-    ptx::mbar_arrive_expect_tx(&sm.bar, Sh::TILE);
 #pragma unroll
-    for (int m = 0; m < Sh::NBOX; ++m) {
-      ptx::tma_load_4d(tile + m * DIM * 128, &state_map, &sm.bar, m * BOXW, 0, hv, static_cast<int32_t>(slot));
+    for (int qt = 0; qt < Sh::NQ; ++qt) ptx::mbar_init(&sm.bar[qt], 1);
+    ptx::fence_mbar_init();
+    // quarter by quarter, so the first rows can be folded while the rest fly
+#pragma unroll
+    for (int qt = 0; qt < Sh::NQ; ++qt) {
+      ptx::mbar_arrive_expect_tx(&sm.bar[qt], Sh::NBOX * 32 * 128);
+#pragma unroll
+      for (int m = 0; m < Sh::NBOX; ++m) {
+        ptx::tma_load_4d(tile + m * DIM * 128 + qt * 32 * 128, &state_map, &sm.bar[qt], m * BOXW, qt * 32, hv,
+                         static_cast<int32_t>(slot));
+      }
     }
   }
 
@@ -322,17 +347,63 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
   }
   __syncthreads();  // coefficients visible
 
-  // ---- wait for the tile ----------------------------------------------------- //
-  if (!ptx::mbar_wait_bounded(&sm.bar, 0, kWaitLimitNs)) {
-    if (tid == 0) atomicExch(p.status, kStatusTmaTimeout);
-    ptx::mbar_wait_bounded(&sm.bar, 0, kWaitLimitNs);  // let an in-flight copy land before exiting
-    return;
+  // ---- wait for this warp's 32-row quarter of the tile ---------------------- //
+  {
+    const int qt = (warp * 4 * R) / 32;
+    if (!ptx::mbar_wait_bounded(&sm.bar[qt], 0, kWaitLimitNs)) {
+      if (lane == 0) atomicExch(p.status, kStatusTmaTimeout);
+      ptx::mbar_wait_bounded(&sm.bar[qt], 0, kWaitLimitNs);  // let an in-flight copy land before exiting
+      return;
+    }
   }
 
   // ---- one pass over S_0: thread = R rows x 1/8 of K --------------------------- //
   const int kg = lane & 7;                  // K-group: chunk kg of every box
   const int r0 = (warp * 4 + (lane >> 3)) * R;  // first row of this thread
   float acc[V];
+#if GDN_RSSM_VERIFY_PACKED_FMA
+  // accumulators hold (even-k, odd-k) partial sums as packed f32 pairs
+  unsigned long long acc2[R][NJ];
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc2[a][j] = 0ull;
+#pragma unroll
+  for (int m = 0; m < Sh::NBOX; ++m) {
+    unsigned long long sp[R][EPC / 2];
+#pragma unroll
+    for (int a = 0; a < R; ++a) {
+      const int r = r0 + a;
+      const uint4 raw = *reinterpret_cast<const uint4 *>(tile + m * DIM * 128 + r * 128 + ((kg ^ (r & 7)) << 4));
+      if constexpr (sizeof(St) == 4) {
+        sp[a][0] = (static_cast<unsigned long long>(raw.y) << 32) | raw.x;
+        sp[a][1] = (static_cast<unsigned long long>(raw.w) << 32) | raw.z;
+      } else {
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sp[a][u] = pack2(__uint_as_float(w4[u] << 16), __uint_as_float(w4[u] & 0xffff0000u));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+#pragma unroll
+      for (int e4 = 0; e4 < EPC / 4; ++e4) {
+        const ulonglong2 xx = *reinterpret_cast<const ulonglong2 *>(&X[j][m * BOXW + e4 * 32 + kg * 4]);
+#pragma unroll
+        for (int a = 0; a < R; ++a) {
+          acc2[a][j] = ffma2(sp[a][e4 * 2 + 0], xx.x, acc2[a][j]);
+          acc2[a][j] = ffma2(sp[a][e4 * 2 + 1], xx.y, acc2[a][j]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+      acc[a * NJ + j] = __uint_as_float(static_cast<uint32_t>(acc2[a][j])) +
+                        __uint_as_float(static_cast<uint32_t>(acc2[a][j] >> 32));
+#else
 #pragma unroll
   for (int a = 0; a < V; ++a) acc[a] = 0.f;
 #pragma unroll
@@ -372,6 +443,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
       }
     }
   }
+#endif
   // ---- reduce the 8 K-groups and gather each row's 2Q sums ----------------- //
   constexpr bool SCATTER = V >= 8;              // else a plain all-reduce
   constexpr int C = SCATTER ? V / 8 : V;        // values held after the scatter
@@ -383,19 +455,30 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
     reduce_scatter<V, 4>(acc, lane);
     // lane kg now holds flat indices [kg*C, kg*C + C): row kg*C/NJ, j from (kg*C)%NJ
     my_row = (kg * C) / NJ;
-    const int jbase = (kg * C) % NJ;
+    if constexpr (LPR == 2) {
+      // even lanes hold the row's k-dots (j < Q), odd lanes its q-dots: swap halves
+      const bool even = (kg & 1) == 0;
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      float v = 0.f;
+      for (int j = 0; j < C; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, acc[j], 1);
+        pr[j] = even ? acc[j] : other;
+        pr[C + j] = even ? other : acc[j];
+      }
+    } else {
+      const int jbase = (kg * C) % NJ;
 #pragma unroll
-      for (int c = 0; c < C; ++c)
-        if (j == jbase + c) v = acc[c];
-      pr[j] = v;
-    }
+      for (int j = 0; j < NJ; ++j) {
+        float v = 0.f;
 #pragma unroll
-    for (int o = 1; o < LPR; o <<= 1) {
+        for (int c = 0; c < C; ++c)
+          if (j == jbase + c) v = acc[c];
+        pr[j] = v;
+      }
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) pr[j] += __shfl_xor_sync(0xffffffffu, pr[j], o);
+      for (int o = 1; o < LPR; o <<= 1) {
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) pr[j] += __shfl_xor_sync(0xffffffffu, pr[j], o);
+      }
     }
     writer_out = (kg % LPR) == LPR - 1;
     writer_corr = (kg % LPR) == 0;
