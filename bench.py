@@ -45,15 +45,15 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _traffic_profile(cfg):
-    """Per-launch DRAM traffic of the fold kernel from the committed ncu
-    summary (scaled to this workload's units), or None."""
+def _traffic_profile(cfg, reduced):
+    """Per-launch DRAM traffic (bytes) of the fold kernel at this config's full
+    size, from the committed ncu summary; None for reduced workloads or when
+    no capture exists."""
     p = ROOT / "profiles" / "traffic.json"
-    if not p.exists():
+    if reduced or not p.exists():
         return None
-    d = json.loads(p.read_text())
-    entry = d.get(f"fold_config{cfg}")
-    return entry
+    entry = json.loads(p.read_text()).get(f"fold_config{cfg}")
+    return int(entry) if entry is not None else None
 
 
 class ClockSampler:
@@ -282,7 +282,7 @@ def run_b200(args):
     fold_gbs = fbytes / (fold_ms * 1e-3) / 1e9
     verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
     step_gbs = (vbytes + fbytes) / (step_ms * 1e-3) / 1e9
-    traffic = _traffic_profile(args.config)
+    traffic = _traffic_profile(args.config, args.rows is not None or args.pool is not None)
     value = wl.B / (step_ms * 1e-3)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,

@@ -45,6 +45,7 @@ const char *get_error();
 // reads and clears all of them).
 constexpr int32_t kStatusTmaTimeout = 1;
 constexpr int32_t kStatusMisaligned = 2;
+constexpr int32_t kStatusMmaTimeout = 4;
 
 // Resolve (once per device) the device address of a translation unit's status
 // word; GetSymbol wraps cudaGetSymbolAddress for that word.

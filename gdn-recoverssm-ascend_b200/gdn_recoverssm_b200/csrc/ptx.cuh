@@ -98,3 +98,113 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 
 }  // namespace ptx
 }  // namespace gdn_rssm
+
+// ---- tcgen05: 5th-generation tensor cores with tensor-memory accumulators --
+namespace gdn_rssm {
+namespace ptx {
+
+// Warp-wide: allocate `ncols` (power of two >= 32) tensor-memory columns and
+// write their base address to shared memory.
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+
+// Warp-wide: this CTA allocates no more tensor memory.
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+// Warp-wide (the allocating warp): free the columns.
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Order tcgen05 operations around a thread synchronisation.
+__device__ __forceinline__ void tc_fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (tensor-core operand reads, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand stored in 128-byte
+// swizzle atoms (8 rows x 128 bytes, 1024-byte aligned, rows 128 bytes apart,
+// 16-byte chunk c of row r at chunk c ^ (r % 8)).  `addr` may point 32, 64 or
+// 96 bytes into the first row to select a K sub-block.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3fffu);  // start address, 16-byte units
+  d |= static_cast<uint64_t>(1) << 16;                // leading byte offset (unused when swizzled)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;        // stride byte offset: next 8-row group
+  d |= static_cast<uint64_t>(1) << 46;                // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;                // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: D (f32) += A (tf32, K-major, M rows) x B^T (tf32,
+// K-major, N rows).
+template <int M, int N>
+__host__ __device__ constexpr uint32_t tf32_instr_desc() {
+  static_assert(M == 128 && N % 16 == 0 && N >= 16 && N <= 256, "tf32 MMA shape");
+  return (1u << 4)                                 // accumulator f32
+         | (2u << 7)                               // A tf32
+         | (2u << 10)                              // B tf32
+         | (static_cast<uint32_t>(N >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);  // M / 16
+}
+
+// One thread: D[tmem] (+)= A x B^T, K = 8 (32 bytes of each operand row).
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(static_cast<uint32_t>(accumulate))
+      : "memory");
+}
+
+// Arrive (once) on `bar` when every tcgen05 operation this thread issued so
+// far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// Warp-wide: lane i reads NCOL (16 or 32) consecutive 32-bit columns of
+// tensor-memory lane (lane base of `taddr`) + i.  The wait for the load is in
+// the same asm statement, so no use of the outputs can be scheduled before
+// the data has arrived.
+template <int NCOL>
+__device__ __forceinline__ void tmem_ld_sync(uint32_t taddr, float *v) {
+  static_assert(NCOL == 16 || NCOL == 32, "tcgen05.ld width");
+  uint32_t r[NCOL];
+  if constexpr (NCOL == 16) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+  }
+#pragma unroll
+  for (int i = 0; i < NCOL; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace ptx
+}  // namespace gdn_rssm

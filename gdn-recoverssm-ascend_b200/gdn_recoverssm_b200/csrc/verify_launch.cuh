@@ -4,7 +4,10 @@
 // status word.
 #pragma once
 
+#include <type_traits>
+
 #include "verify.cuh"
+#include "verify_tc.cuh"
 
 namespace gdn_rssm {
 
@@ -22,13 +25,32 @@ struct VerifyLaunch {
 int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, int dim, int64_t value_heads,
                      int64_t blocks, int64_t state_bs, int64_t state_hs, int64_t state_vs);
 
+// K = V = 128 with an fp32 pool runs the tensor-core kernel (verify_tc.cuh);
+// other shapes the CUDA-core kernel (verify.cuh).
+#ifndef GDN_RSSM_VERIFY_TENSOR_CORES
+#define GDN_RSSM_VERIFY_TENSOR_CORES 1
+#endif
+
+template <int DIM, typename St>
+constexpr bool verify_uses_tensor_cores() {
+  return GDN_RSSM_VERIFY_TENSOR_CORES && DIM == 128 && std::is_same<St, float>::value;
+}
+
 template <int DIM, int QT, typename Act, typename St>
 int launch_verify_variant(VerifyLaunch &L) {
   CUtensorMap map;
   int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, L.p.value_heads, L.p.blocks, L.state_bs, L.state_hs,
                             L.state_vs);
   if (rc != GDN_RSSM_OK) return rc;
-  constexpr int smem = verify_smem_bytes<DIM, QT, Act, St>();
+  constexpr bool tc = verify_uses_tensor_cores<DIM, St>();
+  constexpr int smem = tc ? verify_tc_smem_bytes<QT, Act>() : verify_smem_bytes<DIM, QT, Act, St>();
+  auto kernel = [] {
+    if constexpr (tc) {
+      return verify_tc_kernel<QT, Act>;
+    } else {
+      return verify_kernel<DIM, QT, Act, St>;
+    }
+  }();
   static bool configured[64] = {false};
   int dev = 0;
   GDN_CUDA(cudaGetDevice(&dev));
@@ -37,12 +59,12 @@ int launch_verify_variant(VerifyLaunch &L) {
     return GDN_RSSM_EUNSUPPORTED;
   }
   if (!configured[dev]) {
-    GDN_CUDA(cudaFuncSetAttribute(verify_kernel<DIM, QT, Act, St>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    GDN_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev] = true;
   }
   // one CTA per (row, value head) unit
   const int64_t grid = L.p.rows * L.p.value_heads;
-  verify_kernel<DIM, QT, Act, St><<<static_cast<unsigned>(grid), kVerifyThreads, smem, L.stream>>>(map, L.p);
+  kernel<<<static_cast<unsigned>(grid), kVerifyThreads, smem, L.stream>>>(map, L.p);
   GDN_CUDA(cudaGetLastError());
   return GDN_RSSM_OK;
 }

@@ -36,8 +36,12 @@ def _rel(got, want):
 
 
 def _bf16_ok(got, want):
+    """[Q, V] bf16 outputs of one unit: within one bf16 ulp of the float64
+    value, or within 1e-5 of the token's largest output magnitude (near-zero
+    results of a cancelling sum)."""
     ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(want), 1e-30))) - 7)
-    return bool(np.all(np.abs(got - want) <= ulp * 1.01 + 1e-30))
+    floor = 1e-5 * np.abs(want).max(axis=-1, keepdims=True)
+    return bool(np.all(np.abs(got - want) <= np.maximum(ulp * 1.01, floor) + 1e-30))
 
 
 def _sample_units(B, HV, n, seed):

@@ -1,0 +1,150 @@
+"""GPU parity of verify at the production head size K = V = 128.
+
+With an fp32 state pool this shape runs the tensor-core kernel (tcgen05 MMAs
+on a three-product tf32 split of S and X); with a bf16 pool the CUDA-core
+kernel.  Every case is checked element by element against the float64 oracle
+(oracle.gdn_oracle.verify_batch), with the edge cases the reference kernel
+masks: ragged windows (qlen 0 .. Q), a window running past the last token,
+null / negative / out-of-pool slots, rows past ``record_rows``, GQA, packed and
+typed records, in-kernel q/k normalisation, every window template (Q = 1, 2,
+3..4, 5..8) and every activation dtype.  State values carry all 23 mantissa
+bits and span four decades, so a tf32 product that lost its low part would
+miss the 1e-5 bound by two orders of magnitude.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn_oracle as O
+from tests.test_gpu_parity import assert_fp32_close
+
+pytestmark = pytest.mark.gpu
+D = 128
+
+CASES = [
+    # Q, activation, record layout, normalise in kernel, H, HV, state dtype
+    (1, torch.bfloat16, "packed", False, 2, 4, torch.float32),
+    (2, torch.bfloat16, "soa", True, 2, 4, torch.float32),
+    (3, torch.float32, "packed", True, 2, 4, torch.float32),
+    (4, torch.bfloat16, "packed", False, 2, 4, torch.float32),
+    (4, torch.float16, "soa", False, 1, 4, torch.float32),
+    (5, torch.bfloat16, "packed", True, 2, 4, torch.float32),
+    (8, torch.bfloat16, "soa", False, 2, 4, torch.float32),
+    (8, torch.float32, "packed", False, 4, 4, torch.float32),
+    (4, torch.bfloat16, "packed", False, 2, 4, torch.bfloat16),
+]
+
+
+@pytest.fixture(scope="module")
+def pkg():
+    import gdn_recoverssm_b200 as g
+    from gdn_recoverssm_b200 import _native
+
+    _native.ops()
+    return g
+
+
+def _case(seed, Q, act, H, HV, state_dtype, normalize, rows=12, blocks=16):
+    rng = np.random.default_rng(seed)
+    qlen = rng.integers(0, Q + 1, rows)
+    qlen[0], qlen[1] = Q, 0
+    qsl = np.concatenate([[0], np.cumsum(qlen)]).astype(np.int32)
+    T = max(int(qsl[-1]) - 1, 1)  # the last row's final token lies past T: masked
+    slots = rng.permutation(np.arange(1, blocks))[:rows].astype(np.int32)
+    slots[2], slots[3], slots[4] = 0, blocks, -1  # null, out of pool, negative
+    q = rng.standard_normal((T, H, D))
+    k = rng.standard_normal((T, H, D))
+    if not normalize:
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((T, HV, D))
+    g = -np.log1p(np.exp(rng.standard_normal((T, HV))))
+    beta = 1.0 / (1.0 + np.exp(-rng.standard_normal((T, HV))))
+    scale_rows = 10.0 ** rng.uniform(-2, 2, (blocks, HV, D, 1))
+    state = rng.standard_normal((blocks, HV, D, D)) * 0.1 * scale_rows
+    t = dict(
+        q=torch.tensor(q, dtype=act), k=torch.tensor(k, dtype=act), v=torch.tensor(v, dtype=act),
+        g=torch.tensor(g, dtype=torch.float32), beta=torch.tensor(beta, dtype=torch.float32),
+        state=torch.tensor(state, dtype=torch.float32).to(state_dtype),
+        qsl=torch.tensor(qsl), slots=torch.tensor(slots),
+    )
+    return t
+
+
+def _assert_rounded_close(got, want, mantissa_bits, min_normal_exp, what):
+    """[T, HV, V] low-precision outputs: each element within one ulp of the
+    float64 oracle value (subnormal ulp below the normal range), or within
+    the fp32 tolerance (1e-5) of its (token, head) output vector's largest
+    magnitude -- the floor for near-zero outputs of a cancelling 128-term sum,
+    which no fp32 computation pins to the ulp of the result."""
+    live = want != -23.0
+    expo = np.maximum(np.floor(np.log2(np.maximum(np.abs(want), 1e-300))), min_normal_exp)
+    ulp = np.exp2(expo - mantissa_bits)
+    vmax = np.abs(np.where(live, want, 0.0)).max(axis=-1, keepdims=True)
+    ok = (np.abs(got - want) <= ulp * 1.01) | (np.abs(got - want) <= 1e-5 * vmax)
+    assert np.all(ok | ~live), f"{what}: {int((~ok & live).sum())} elements off"
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"Q{c[0]}-{str(c[1])[6:]}-{c[2]}-n{int(c[3])}-H{c[4]}-{str(c[6])[6:]}")
+def test_verify_k128_matches_oracle(pkg, case):
+    Q, act, layout, normalize, H, HV, state_dtype = case
+    c = _case(1234 + Q, Q, act, H, HV, state_dtype, normalize)
+    T = c["q"].shape[0]
+    rows = c["slots"].shape[0]
+    R = rows - 2  # the last two rows have no record row
+    dev = {n: x.cuda() for n, x in c.items()}
+    out = torch.full((1, T, HV, D), -23.0, dtype=act, device="cuda")
+    if layout == "packed":
+        cache = torch.full((R, HV, Q, 2 * D + 1), -17.0, device="cuda")
+    else:
+        kd = torch.float32 if normalize else act
+        cache = pkg.ReplayRecordBuffers(
+            torch.full((R, HV, Q, D), -17.0, device="cuda"),
+            torch.full((R, H, Q, D), -16.0, dtype=kd, device="cuda"),
+            torch.full((R, HV, Q), -19.0, device="cuda"),
+        )
+    before = dev["state"].clone()
+    pkg.gdn_recoverssm_verify(
+        dev["g"][None], dev["beta"][None], dev["q"][None], dev["k"][None], dev["v"][None],
+        checkpoint_state=dev["state"], replay_cache=cache, query_start_loc=dev["qsl"], state_indices=dev["slots"],
+        spec_query_len=Q, qk_already_normalized=not normalize, out=out,
+    )
+    torch.cuda.synchronize()
+    assert torch.equal(dev["state"], before), "verify modified the read-only checkpoint"
+    assert int(torch.ops.gdn_recoverssm_ac.device_status()) == 0
+
+    f64 = lambda x: x.double().numpy()
+    o_out = np.full((T, HV, D), -23.0)
+    if layout == "packed":
+        o_rec = np.full((R, HV, Q, 2 * D + 1), -17.0)
+    else:
+        o_rec = (np.full((R, HV, Q, D), -17.0), np.full((R, H, Q, D), -16.0), np.full((R, HV, Q), -19.0))
+    O.verify_batch(f64(c["q"]), f64(c["k"]), f64(c["v"]), f64(c["g"]), f64(c["beta"]), f64(c["state"]),
+                   c["qsl"].numpy(), c["slots"].numpy(), spec_query_len=Q, normalize_qk=normalize, record_rows=R,
+                   layout=layout, out=o_out, records=o_rec)
+
+    got = out[0].double().cpu().numpy()
+    assert np.array_equal(got == -23.0, o_out == -23.0), "output store mask"
+    live = o_out != -23.0
+    if act == torch.float32:
+        assert_fp32_close(got[live], o_out[live], what="output")
+    elif act == torch.bfloat16:
+        _assert_rounded_close(got, o_out, 7, -126, "bf16 output")
+    else:
+        _assert_rounded_close(got, o_out, 10, -14, "f16 output")
+    if layout == "packed":
+        rec = cache.double().cpu().numpy()
+        assert np.array_equal(rec == -17.0, o_rec == -17.0), "record store mask"
+        m = o_rec != -17.0
+        assert_fp32_close(rec[m], o_rec[m], what="packed records")
+    else:
+        for got_t, want, sentinel, name in zip((cache.correction, cache.key, cache.decay), o_rec, (-17.0, -16.0, -19.0),
+                                              ("correction", "key", "decay")):
+            g_np = got_t.double().cpu().numpy()
+            assert np.array_equal(g_np == sentinel, want == sentinel), f"{name} store mask"
+            m = want != sentinel
+            if name == "key" and not normalize:
+                assert np.array_equal(g_np[m], want[m]), "pre-normalised keys keep their input bits"
+            else:
+                assert_fp32_close(g_np[m], want[m], what=name)
