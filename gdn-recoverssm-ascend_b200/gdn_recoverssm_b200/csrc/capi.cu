@@ -59,8 +59,8 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, int dim, int64_t value_heads,
-                     int64_t blocks, int64_t state_bs, int64_t state_hs, int64_t state_vs) {
+int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, int dim, int box_rows,
+                     int64_t value_heads, int64_t blocks, int64_t state_bs, int64_t state_hs, int64_t state_vs) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) {
     set_error("GDN RecoverSSM: cuTensorMapEncodeTiled is unavailable from the driver");
@@ -71,9 +71,8 @@ int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, in
                               static_cast<cuuint64_t>(value_heads), static_cast<cuuint64_t>(blocks)};
   const cuuint64_t gstride[3] = {static_cast<cuuint64_t>(state_vs * es), static_cast<cuuint64_t>(state_hs * es),
                                  static_cast<cuuint64_t>(state_bs * es)};
-  // one box = 128 bytes of K x 32 rows (the verify kernel loads the tile in
-  // 32-row quarters, each on its own mbarrier)
-  const cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), 32u, 1, 1};
+  // one box = 128 bytes of K (one swizzle row) x box_rows rows
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(box_rows), 1, 1};
   const cuuint32_t estride[4] = {1, 1, 1, 1};
   const CUresult r = fn(map,
                         state_dtype == GDN_RSSM_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,

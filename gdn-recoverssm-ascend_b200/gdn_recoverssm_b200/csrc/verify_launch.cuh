@@ -4,6 +4,7 @@
 // status word.
 #pragma once
 
+#include <algorithm>
 #include <type_traits>
 
 #include "verify.cuh"
@@ -22,8 +23,9 @@ struct VerifyLaunch {
 };
 
 // Encodes the 4-D tiled tensor map of the state pool (defined in capi.cu).
-int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, int dim, int64_t value_heads,
-                     int64_t blocks, int64_t state_bs, int64_t state_hs, int64_t state_vs);
+// Box: 128 bytes of K x box_rows rows.
+int encode_state_map(CUtensorMap *map, const void *base, int32_t state_dtype, int dim, int box_rows,
+                     int64_t value_heads, int64_t blocks, int64_t state_bs, int64_t state_hs, int64_t state_vs);
 
 // K = V = 128 with an fp32 pool runs the tensor-core kernel (verify_tc.cuh);
 // other shapes the CUDA-core kernel (verify.cuh).
@@ -38,11 +40,13 @@ constexpr bool verify_uses_tensor_cores() {
 
 template <int DIM, int QT, typename Act, typename St>
 int launch_verify_variant(VerifyLaunch &L) {
-  CUtensorMap map;
-  int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, L.p.value_heads, L.p.blocks, L.state_bs, L.state_hs,
-                            L.state_vs);
-  if (rc != GDN_RSSM_OK) return rc;
   constexpr bool tc = verify_uses_tensor_cores<DIM, St>();
+  // tensor-core kernel: whole-height boxes (4 copies per tile); CUDA-core
+  // kernel: 32-row quarters, each on its own mbarrier
+  CUtensorMap map;
+  int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, tc ? DIM : 32, L.p.value_heads, L.p.blocks,
+                            L.state_bs, L.state_hs, L.state_vs);
+  if (rc != GDN_RSSM_OK) return rc;
   constexpr int smem = tc ? verify_tc_smem_bytes<QT, Act>() : verify_smem_bytes<DIM, QT, Act, St>();
   auto kernel = [] {
     if constexpr (tc) {
@@ -62,8 +66,14 @@ int launch_verify_variant(VerifyLaunch &L) {
     GDN_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev] = true;
   }
-  // one CTA per (row, value head) unit
-  const int64_t grid = L.p.rows * L.p.value_heads;
+  const int64_t units = L.p.rows * L.p.value_heads;
+  if (units <= 0) return GDN_RSSM_OK;
+  int64_t grid = units;  // CUDA-core kernel: one CTA per (row, value head) unit
+  if constexpr (tc) {
+    // tensor-core kernel: as many CTAs as fit at once, each walking units
+    // blockIdx.x + k * gridDim.x
+    grid = std::min<int64_t>(units, static_cast<int64_t>(sm_count_current_device()) * verify_tc_min_blocks<QT>());
+  }
   kernel<<<static_cast<unsigned>(grid), kVerifyThreads, smem, L.stream>>>(map, L.p);
   GDN_CUDA(cudaGetLastError());
   return GDN_RSSM_OK;
