@@ -209,6 +209,31 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// Instruction descriptor: D (f32) += A (bf16, K-major, M rows) x B^T (bf16,
+// K-major, N rows), K = 16 per instruction.
+template <int M, int N>
+__host__ __device__ constexpr uint32_t bf16_instr_desc() {
+  static_assert(M == 128 && N % 16 == 0 && N >= 16 && N <= 256, "bf16 MMA shape");
+  return (1u << 4)                                 // accumulator f32
+         | (1u << 7)                               // A bf16
+         | (1u << 10)                              // B bf16
+         | (static_cast<uint32_t>(N >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);  // M / 16
+}
+
+// One thread: D[tmem] (+)= A[tmem] x B^T, A = 128 lanes x 8 columns of packed
+// bf16 pairs (K = 16, element 2c in the low half of column c) in tensor
+// memory, B in shared memory.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(static_cast<uint32_t>(accumulate))
+      : "memory");
+}
+
 // One thread: D[tmem] (+)= A[tmem] x B^T with A (128 lanes x 8 tf32 columns
 // from `a_tmem`) in tensor memory and B in shared memory, K = 8.
 __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -253,6 +278,14 @@ __device__ __forceinline__ void tmem_ld_sync(uint32_t taddr, float *v) {
   }
 #pragma unroll
   for (int i = 0; i < NCOL; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// As tmem_st32, from raw 32-bit words.
+__device__ __forceinline__ void tmem_st32_u(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 // Warp-wide: lane i writes 32 consecutive 32-bit columns of tensor-memory lane

@@ -22,12 +22,14 @@
 // blockIdx.x, blockIdx.x + gridDim.x, ...; per unit:
 //   all:      stage hi/lo(X) into B, g / beta, decay and key records (the
 //             unit's q/k/v/g/beta were loaded into registers during the
-//             previous unit, its slot two units back); Gram coefficients
-//             while the tile is in flight;
-//   thread 0: MMA pass 1 -> commit; all: rewrite the tile as lo(S);
-//   thread 0: MMA pass 2 -> commit, then at once the TMA of the NEXT unit's
-//             tile (4-D tensor map, 128-byte swizzle: the layout the MMA's
-//             K-major descriptor reads directly) into the freed buffer;
+//             previous unit) while the tile is in flight;
+//   thread 0: MMA pass 1 -> commit; meanwhile all threads compute the Gram
+//             coefficients and start the loads of the next units' slots and
+//             activations;
+//   all:      rewrite the tile as lo(S); thread 0: MMA pass 2 -> commit, then
+//             at once the TMA of the NEXT unit's tile (4-D tensor map,
+//             128-byte swizzle: the layout the MMA's K-major descriptor reads
+//             directly, one 128-row box per K slab) into the freed buffer;
 //   all:      every warp loads its 32 rows' sums from tensor memory (one row
 //             per lane) and runs the recurrence -- warps 0-3 write the
 //             correction records, warps 4-7 the outputs -- while that load
@@ -46,7 +48,10 @@ struct VerifyTcShape {
   static constexpr int DIM = 128;
   static constexpr int NJ = 2 * QT;                    // dot products per state row
   static constexpr int NB = (2 * NJ + 15) / 16 * 16;   // B operand rows: hi(X), lo(X), zero padding
-  static constexpr int TMEM_COLS = 32;                 // accumulator columns (>= NB, power of two)
+  static constexpr int TMEM_COLS = 128;                // accumulator + bf16 lo(S)
+  static constexpr uint32_t D_COL = 0;                 // accumulator: NB columns
+  static constexpr uint32_t A_LO = 64;                 // bf16 lo(S): 64 columns of packed pairs
+  static constexpr int NB2 = 16;                       // rows of the pass-2 B operand (bf16 X, zero padded)
   static constexpr int SLAB = DIM * 128;               // one 32-column K slab of the tile (bytes)
   static constexpr int TILE = DIM * DIM * 4;
   static constexpr int B_SLAB = NB * 128;
@@ -65,7 +70,8 @@ struct VerifyTcShape {
     Window win[2];
   };
   static constexpr int SMEM = 1024 /* alignment slack */ + TILE + B_BYTES + static_cast<int>(sizeof(Small));
-  static_assert(NB <= TMEM_COLS && (NB == 16 || NB == 32), "accumulator columns");
+  static_assert(NB <= static_cast<int>(A_LO) && (NB == 16 || NB == 32), "accumulator columns");
+  static_assert(NJ <= NB2 && 2 * NB2 * 128 <= B_BYTES, "pass-2 B operand reuses the B buffer");
   static_assert(B_SLAB % 1024 == 0, "B operand slabs must stay 1024-byte aligned");
 };
 
@@ -279,9 +285,12 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   bool ok = true;
 
   for (int64_t u = blockIdx.x, i = 0; u < units && ok; u += G, ++i) {
-    const TcUnitMeta m2 = load_meta(c2, u + 2 * G < units);  // two units ahead
-    Inputs in;
-    load_inputs(in, c1, m1);                                  // one unit ahead
+    TcUnitMeta m2;  // two units ahead
+    Inputs in;      // one unit ahead
+    auto prefetch = [&]() {
+      m2 = load_meta(c2, u + 2 * G < units);
+      load_inputs(in, c1, m1);
+    };
     const int64_t row = c0.row;
     const int hv = static_cast<int>(c0.hv);
     const int h = hv / ratio;
@@ -291,6 +300,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
 
     if (!is_live(m0)) {
       // ---- null / out-of-pool slot: zero output, nothing loaded ------------ //
+      prefetch();
       for (int e = tid; e < QT * DIM; e += kVerifyThreads) {
         const int t = e / DIM;
         if ((vmask >> t) & 1) out[(m0.bos + t) * p.out_ts + hv * DIM + (e % DIM)] = from_f32<Act>(0.f);
@@ -315,12 +325,13 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
               make_uint4(0u, 0u, 0u, 0u);
         }
       }
+      float xs[PER_WARP][EPL];  // this warp's staged vectors, kept for the pass-2 operand
 #pragma unroll
       for (int c = 0; c < PER_WARP; ++c) {
         const int j = warp + 8 * c;
         if (j >= NJ) continue;
         const int t = j % QT;
-        float x[EPL];
+        float *x = xs[c];
 #pragma unroll
         for (int e = 0; e < EPL; ++e) x[e] = to_f32<Act>(ic.x[c][e]);
         if (normalize) {
@@ -359,17 +370,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
             make_float4(lo[0], lo[1], lo[2], lo[3]);
       }
       ptx::fence_proxy_async_smem();  // B operand -> tensor-core reads
-      __syncthreads();                // B, dec, beta staged
-      gram_coefficients<QT, NJ, Sh::B_SLAB>(bop, w.dec, w.mkk, w.mkq, tid);
-      if (tid == 0) {
-        float a = 1.f;
-#pragma unroll
-        for (int t = 0; t < QT; ++t) {
-          a *= w.dec[t];
-          w.A[t] = a;
-        }
-      }
-      // ---- the tile has landed (every thread: the rewrite reads it) ---------- //
+      // ---- B, dec, beta staged by every thread; the tile has landed ---------- //
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.tile_bar, tile_par, kWaitLimitNs))) {
         if (tid == 0) atomicExch(p.status, kStatusTmaTimeout);
         ptx::mbar_wait_bounded(&sm.tile_bar, tile_par, kWaitLimitNs);  // let an in-flight copy land
@@ -385,10 +386,44 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           const uint32_t sub = (kk & 3) * 32;  // K sub-block (8 tf32) inside the 128-byte row
           const uint64_t a = ptx::sw128_kmajor_desc(tile_addr + (kk >> 2) * Sh::SLAB + sub);
           const uint64_t b = ptx::sw128_kmajor_desc(b_addr + (kk >> 2) * Sh::B_SLAB + sub);
-          ptx::mma_tf32(tmem, a, b, IDESC, kk > 0);
+          ptx::mma_tf32(tmem + Sh::D_COL, a, b, IDESC, kk > 0);
         }
         ptx::mma_commit(&sm.mma_bar);
       }
+      // ---- while pass 1 runs: bf16 lo(S) -> tensor memory ---------------------- //
+      // warp w: rows 32 (w % 4) .. + 31 (one per lane), K elements 64 (w / 4) .. + 63
+      {
+        const int kh = warp >> 2;
+        const unsigned char *row_base = tile + r * 128;
+        uint32_t packed_lo[32];
+#pragma unroll
+        for (int mm = 0; mm < 2; ++mm) {
+          const int m = 2 * kh + mm;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 x = *reinterpret_cast<const float4 *>(row_base + m * Sh::SLAB + ((c ^ (r & 7)) << 4));
+            const __nv_bfloat162 lo01 = __floats2bfloat162_rn(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y));
+            const __nv_bfloat162 lo23 = __floats2bfloat162_rn(x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+            packed_lo[mm * 16 + 2 * c] = *reinterpret_cast<const uint32_t *>(&lo01);
+            packed_lo[mm * 16 + 2 * c + 1] = *reinterpret_cast<const uint32_t *>(&lo23);
+          }
+        }
+        __syncwarp();  // tcgen05.st is warp-wide (.sync.aligned)
+        ptx::tmem_st32_u(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::A_LO + 32u * kh, packed_lo);
+        ptx::tmem_wait_st();
+      }
+      // ---- ... the Gram coefficients and the next units' loads ---------------- //
+      gram_coefficients<QT, NJ, Sh::B_SLAB>(bop, w.dec, w.mkk, w.mkq, tid);
+      if (tid == 0) {
+        float a = 1.f;
+#pragma unroll
+        for (int t = 0; t < QT; ++t) {
+          a *= w.dec[t];
+          w.A[t] = a;
+        }
+      }
+      prefetch();
+      ptx::tc_fence_before_sync();
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
         if (tid == 0) atomicExch(p.status, kStatusMmaTimeout);
         ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs);
@@ -396,31 +431,42 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         break;
       }
       mma_par ^= 1u;
-      // ---- rewrite the tile as lo(S), pass 2 ------------------------------------- //
-      ptx::tc_fence_after_sync();
+      // ---- the tile is read (pass 1 and lo(S)): start the next unit's load ---- //
+      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
+      // ---- pass 2: bf16 lo(S) x bf16(X), B rewritten in place ----------------- //
+      // B2 (NB2 rows, K-major, 128-byte swizzle, 64 bf16 per row and slab): row j
+      // = bf16(x_j) for j < NJ, zero above (those columns hold hi(S) lo(X)).
       {
-        float4 *t4 = reinterpret_cast<float4 *>(tile);
-#pragma unroll 4
-        for (int c = tid; c < Sh::TILE / 16; c += kVerifyThreads) {
-          float4 v = t4[c];
-          v.x -= tf32_hi(v.x);
-          v.y -= tf32_hi(v.y);
-          v.z -= tf32_hi(v.z);
-          v.w -= tf32_hi(v.w);
-          t4[c] = v;
+        constexpr int B2_SLAB = Sh::NB2 * 128;
+#pragma unroll
+        for (int c = 0; c < PER_WARP; ++c) {
+          const int j = warp + 8 * c;
+          if (j >= NJ) continue;
+          const __nv_bfloat162 b01 = __floats2bfloat162_rn(xs[c][0], xs[c][1]);
+          const __nv_bfloat162 b23 = __floats2bfloat162_rn(xs[c][2], xs[c][3]);
+          // lane l holds K elements 4l .. 4l + 3: slab l / 16, chunk (l % 16) / 2, half l % 2
+          const int m = lane >> 4, ch = (lane & 15) >> 1;
+          *reinterpret_cast<uint2 *>(bop + m * B2_SLAB + j * 128 + ((ch ^ (j & 7)) << 4) + (lane & 1) * 8) =
+              make_uint2(*reinterpret_cast<const uint32_t *>(&b01), *reinterpret_cast<const uint32_t *>(&b23));
+        }
+        if constexpr (Sh::NB2 > NJ) {
+          constexpr int PAD = (Sh::NB2 - NJ) * 8;  // 16-byte chunks per slab
+          for (int e = tid; e < 2 * PAD; e += kVerifyThreads) {
+            const int m = e / PAD, rem = e % PAD;
+            *reinterpret_cast<uint4 *>(bop + m * B2_SLAB + (NJ + rem / 8) * 128 + ((rem % 8) << 4)) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
         }
       }
-      ptx::fence_proxy_async_smem();  // lo(S) -> tensor-core reads
-      ptx::tc_fence_before_sync();
+      ptx::fence_proxy_async_smem();  // B2 -> tensor-core reads
       __syncthreads();
       if (tid == 0) {
         ptx::tc_fence_after_sync();
+        constexpr uint32_t IDESC2 = ptx::bf16_instr_desc<128, Sh::NB2>();
 #pragma unroll
-        for (int kk = 0; kk < DIM / 8; ++kk) {
-          const uint32_t sub = (kk & 3) * 32;
-          const uint64_t a = ptx::sw128_kmajor_desc(tile_addr + (kk >> 2) * Sh::SLAB + sub);
-          const uint64_t b = ptx::sw128_kmajor_desc(b_addr + (kk >> 2) * Sh::B_SLAB + sub);
-          ptx::mma_tf32(tmem, a, b, IDESC, true);
+        for (int kk = 0; kk < DIM / 16; ++kk) {
+          const uint64_t b = ptx::sw128_kmajor_desc(b_addr + (kk >> 2) * (Sh::NB2 * 128) + (kk & 3) * 32);
+          ptx::mma_bf16_ts(tmem + Sh::D_COL, tmem + Sh::A_LO + kk * 8, b, IDESC2, true);
         }
         ptx::mma_commit(&sm.mma_bar);
       }
@@ -431,13 +477,11 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         break;
       }
       mma_par ^= 1u;
-      // ---- the tile buffer is free: start the next unit's load --------------- //
-      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
       // ---- per-row recurrence: lane = state row of the warp's lane quadrant --- //
       ptx::tc_fence_after_sync();
       float d[NB];
       __syncwarp();  // tcgen05.ld is warp-wide (.sync.aligned)
-      ptx::tmem_ld_sync<NB>(tmem + (static_cast<uint32_t>(qd * 32) << 16), d);
+      ptx::tmem_ld_sync<NB>(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::D_COL, d);
       ptx::tc_fence_before_sync();
       const bool writer_corr = warp < 4;
       float cr[QT];
