@@ -265,10 +265,10 @@ def run_b200(args):
     plan_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
     fold_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
     step_ms = total_ms / args.steps
-    t = torch.tensor([step_ms, verify_ms, plan_ms, fold_ms, e2e["ms"]], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, verify_ms, plan_ms, fold_ms, e2e_ms = t.tolist()
+    from gdn_recoverssm_b200.sharding import max_over_ranks
+
+    step_ms, verify_ms, plan_ms, fold_ms, e2e_ms = max_over_ranks(
+        [step_ms, verify_ms, plan_ms, fold_ms, e2e["ms"]], device=dev)
     clk = clocks.summary()
     status = int(torch.ops.gdn_recoverssm_ac.device_status())
     if world > 1:

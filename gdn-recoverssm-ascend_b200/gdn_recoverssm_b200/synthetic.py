@@ -28,6 +28,8 @@ from dataclasses import dataclass, field
 
 import torch
 
+from .sharding import head_shard
+
 CONFIGS = {
     0: dict(B=4, H=4, HV=4, D=64, Q=4, pool=8, act=torch.float32, align=False, accept="uniform"),
     1: dict(B=64, H=16, HV=32, D=128, Q=4, pool=256, act=torch.bfloat16, align=False, accept="uniform"),
@@ -154,9 +156,8 @@ def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv
     rank's head shard)."""
     spec = spec_of(cfg, rows, pool)
     B, H, HV, D, Q, pool = spec["B"], spec["H"], spec["HV"], spec["D"], spec["Q"], spec["pool"]
-    if H % world or HV % world:
-        raise ValueError(f"config {cfg}: {H} key / {HV} value heads do not shard over {world} ranks")
-    H, HV = H // world, HV // world
+    shard = head_shard(H, HV, world, rank)
+    H, HV = shard.key_heads, shard.value_heads
     act = spec["act"]
     meta = metadata(cfg, seed, rows, pool)
     dev = torch.device(device)
