@@ -1,6 +1,6 @@
-// Thin inline-PTX wrappers for the sm_100a async-copy machinery used here:
-// shared-memory mbarriers and TMA (cp.async.bulk.tensor) tile loads.  No
-// multicast form is used anywhere in this library.
+// Thin inline-PTX wrappers for the sm_100a machinery used here: shared-memory
+// mbarriers, TMA (cp.async.bulk.tensor) and bulk tile loads into this CTA's
+// own shared memory, and the tcgen05 tensor-core / tensor-memory operations.
 #pragma once
 
 #include <cuda.h>
