@@ -283,6 +283,8 @@ def run_b200(args):
     verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
     step_gbs = (vbytes + fbytes) / (step_ms * 1e-3) / 1e9
     traffic = _traffic_profile(args.config, args.rows is not None or args.pool is not None)
+    if traffic is not None:
+        traffic = int(traffic * wl.units / (synthetic.CONFIGS[args.config]["B"] * synthetic.CONFIGS[args.config]["HV"]))
     value = wl.B / (step_ms * 1e-3)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -299,7 +301,7 @@ def run_b200(args):
             "fold": {"ms": fold_ms, "bytes": fbytes, "GB/s": fold_gbs, "frac": fold_gbs / peak},
             "step": {"GB/s": step_gbs, "frac": step_gbs / peak, "per_rank_bytes": vbytes + fbytes},
         },
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 3 * args.steps * world,  # verify, plan, fold per step on every rank
         "clocks": clk,
         "device_status": status,
     }
