@@ -67,6 +67,7 @@ struct VerifyTcShape {
     uint64_t tile_bar;
     uint64_t mma_bar;
     uint32_t tmem;
+    float gpart[4][QT * QT];  // Gram partial sums per K slab
     Window win[2];
   };
   static constexpr int SMEM = 1024 /* alignment slack */ + TILE + B_BYTES + static_cast<int>(sizeof(Small));
@@ -89,62 +90,71 @@ constexpr int verify_tc_min_blocks() {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 
-// Gram coefficients of the window from the B operand ([hi(X); lo(X)], rows
-// 128 bytes apart in 4 K slabs of B_SLAB bytes, 16-byte chunk c of row n at
-// chunk c ^ (n % 8)), with D[t][s] = prod_{s<r<=t} dec[r]:
+// Gram coefficients of the window, in two steps.
+//
+// gram_partials: called by four warps; warp g covers K slab g of the B operand
+// ([hi(X); lo(X)], rows 128 bytes apart in 4 K slabs of B_SLAB bytes, 16-byte
+// chunk c of row n at chunk c ^ (n % 8)) and lane l its element 32 g + l.
+// Every lane forms x_j = hi + lo (exact) for the 2Q vectors -- one
+// conflict-free read of the operand in all -- and all Q^2 pair products, in
+// the order: k_s . k_t for t = 1..Q-1, s < t, then k_s . q_t for t = 0..Q-1,
+// s <= t.  A reduce-scatter over the warp leaves each pair's slab sum on known
+// lanes, which store part[g][pair].
+template <int QT, int NJ, int B_SLAB>
+__device__ __forceinline__ void gram_partials(const unsigned char *bop, float (*part)[QT * QT], int g, int lane) {
+  constexpr int NP = QT * QT;
+  const unsigned char *slab = bop + g * B_SLAB;
+  const int chunk = lane >> 2, word = (lane & 3) * 4;
+  float x[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int jl = NJ + j;
+    const float hi = *reinterpret_cast<const float *>(slab + j * 128 + ((chunk ^ (j & 7)) << 4) + word);
+    const float lo = *reinterpret_cast<const float *>(slab + jl * 128 + ((chunk ^ (jl & 7)) << 4) + word);
+    x[j] = hi + lo;
+  }
+  float acc[NP];
+  int p = 0;
+#pragma unroll
+  for (int t = 1; t < QT; ++t)
+#pragma unroll
+    for (int s2 = 0; s2 < t; ++s2) acc[p++] = x[s2] * x[t];
+#pragma unroll
+  for (int t = 0; t < QT; ++t)
+#pragma unroll
+    for (int s2 = 0; s2 <= t; ++s2) acc[p++] = x[s2] * x[QT + t];
+  reduce_scatter<NP, 16>(acc, lane);
+  if constexpr (NP >= 32) {
+    constexpr int PER = NP / 32;  // lane holds pairs lane * PER .. + PER - 1
+#pragma unroll
+    for (int i = 0; i < PER; ++i) part[g][lane * PER + i] = acc[i];
+  } else {
+    constexpr int SPAN = 32 / NP;  // lanes sharing one pair's sum
+    if (lane % SPAN == 0) part[g][lane / SPAN] = acc[0];
+  }
+}
+
+// gram_finalize: thread `pr` (< Q^2) sums pair pr over the four slabs and
+// scales it by the decay product D[t][s] = prod_{s<r<=t} dec[r]:
 //     mkk[t][s] = D[t][s] (k_s . k_t)  for s < t,
 //     mkq[t][s] = D[t][s] (k_s . q_t)  for s <= t.
-// One task = (pair, part of K): PARTS consecutive lanes split a pair's 32
-// chunks (x = hi + lo, exact) and are summed with log2(PARTS) shuffles; the
-// lanes of a pair start at different chunks so that they read different
-// banks.  Called by the CTA's 256 threads.
-template <int QT, int NJ, int B_SLAB>
-__device__ __forceinline__ void gram_coefficients(const unsigned char *bop, const float *dec, float (*mkk)[QT],
-                                                  float (*mkq)[QT], int tid) {
-  constexpr int SPREAD = kVerifyThreads / (QT * QT);
-  constexpr int PARTS = SPREAD >= 32 ? 32 : SPREAD >= 16 ? 16 : SPREAD >= 8 ? 8 : SPREAD >= 4 ? 4 : 2;
-  constexpr int CPP = 32 / PARTS;  // chunks per lane
+template <int QT>
+__device__ __forceinline__ void gram_finalize(const float (*part)[QT * QT], const float *dec, float (*mkk)[QT],
+                                              float (*mkq)[QT], int pr) {
   constexpr int NKK = QT * (QT - 1) / 2;
-  constexpr int TASKS = QT * QT * PARTS;
-  constexpr int ROUNDED = (TASKS + 31) / 32 * 32;  // whole warps take part in the shuffles
-  for (int task = tid; task < ROUNDED; task += kVerifyThreads) {
-    const bool live = task < TASKS;
-    const int pr = live ? task / PARTS : 0, part = task % PARTS;
-    const int kind = pr >= NKK ? 1 : 0;
-    int rem = kind ? pr - NKK : pr, t = 0;
-    while (rem >= (kind ? t + 1 : t)) {
-      rem -= kind ? t + 1 : t;
-      ++t;
-    }
-    const int s2 = rem;
-    const int a = s2, b = kind ? QT + t : t;
-    const int sa = a & 7, sla = (NJ + a) & 7, sb = b & 7, slb = (NJ + b) & 7;
-    float acc = 0.f;
-#pragma unroll 4
-    for (int i = 0; i < CPP; ++i) {
-      const int g = part * CPP + ((i + part) % CPP);  // chunk 0..31 of the row: slab g / 8, chunk g % 8
-      const unsigned char *slab = bop + (g >> 3) * B_SLAB;
-      const int c = g & 7;
-      const float4 xa = *reinterpret_cast<const float4 *>(slab + a * 128 + ((c ^ sa) << 4));
-      const float4 ya = *reinterpret_cast<const float4 *>(slab + (NJ + a) * 128 + ((c ^ sla) << 4));
-      const float4 xb = *reinterpret_cast<const float4 *>(slab + b * 128 + ((c ^ sb) << 4));
-      const float4 yb = *reinterpret_cast<const float4 *>(slab + (NJ + b) * 128 + ((c ^ slb) << 4));
-      acc = fmaf(xa.x + ya.x, xb.x + yb.x, acc);
-      acc = fmaf(xa.y + ya.y, xb.y + yb.y, acc);
-      acc = fmaf(xa.z + ya.z, xb.z + yb.z, acc);
-      acc = fmaf(xa.w + ya.w, xb.w + yb.w, acc);
-    }
-#pragma unroll
-    for (int o = 1; o < PARTS; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (live && part == 0) {
-      float d = 1.f;
-      for (int r2 = s2 + 1; r2 <= t; ++r2) d *= dec[r2];
-      if (kind == 0) {
-        mkk[t][s2] = d * acc;
-      } else {
-        mkq[t][s2] = d * acc;
-      }
-    }
+  const float sum = (part[0][pr] + part[1][pr]) + (part[2][pr] + part[3][pr]);
+  const int kind = pr >= NKK ? 1 : 0;
+  int rem = kind ? pr - NKK : pr, t = kind ? 0 : 1;
+  while (rem >= (kind ? t + 1 : t)) {
+    rem -= kind ? t + 1 : t;
+    ++t;
+  }
+  float d = 1.f;
+  for (int r2 = rem + 1; r2 <= t; ++r2) d *= dec[r2];
+  if (kind == 0) {
+    mkk[t][rem] = d * sum;
+  } else {
+    mkq[t][rem] = d * sum;
   }
 }
 
@@ -412,16 +422,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         ptx::tmem_st32_u(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::A_LO + 32u * kh, packed_lo);
         ptx::tmem_wait_st();
       }
-      // ---- ... the Gram coefficients and the next units' loads ---------------- //
-      gram_coefficients<QT, NJ, Sh::B_SLAB>(bop, w.dec, w.mkk, w.mkq, tid);
-      if (tid == 0) {
-        float a = 1.f;
-#pragma unroll
-        for (int t = 0; t < QT; ++t) {
-          a *= w.dec[t];
-          w.A[t] = a;
-        }
-      }
+      // ---- ... the Gram partial sums and the next units' loads ---------------- //
+      if (warp >= 4) gram_partials<QT, NJ, Sh::B_SLAB>(bop, sm.gpart, warp - 4, lane);
       prefetch();
       ptx::tc_fence_before_sync();
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
@@ -433,6 +435,16 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       mma_par ^= 1u;
       // ---- the tile is read (pass 1 and lo(S)): start the next unit's load ---- //
       if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
+      // ---- Gram coefficients and decay products of this window ---------------- //
+      if (tid < QT * QT) gram_finalize<QT>(sm.gpart, w.dec, w.mkk, w.mkq, tid);
+      if (tid == 32) {
+        float a = 1.f;
+#pragma unroll
+        for (int t = 0; t < QT; ++t) {
+          a *= w.dec[t];
+          w.A[t] = a;
+        }
+      }
       // ---- pass 2: bf16 lo(S) x bf16(X), B rewritten in place ----------------- //
       // B2 (NB2 rows, K-major, 128-byte swizzle, 64 bf16 per row and slab): row j
       // = bf16(x_j) for j < NJ, zero above (those columns hold hi(S) lo(X)).
