@@ -47,13 +47,17 @@ template <int QT, typename Act>
 struct VerifyTcShape {
   static constexpr int DIM = 128;
   static constexpr int NJ = 2 * QT;                    // dot products per state row
-  static constexpr int NB = (2 * NJ + 15) / 16 * 16;   // B operand rows: hi(X), lo(X), zero padding
-  static constexpr int TMEM_COLS = 128;                // accumulator + bf16 lo(S)
-  static constexpr uint32_t D_COL = 0;                 // accumulator: NB columns
+  static constexpr int NB = (2 * NJ + 15) / 16 * 16;   // pass-1 B rows: hi(X), lo(X), zero padding
+  static constexpr int TMEM_COLS = 128;
+  static constexpr uint32_t D_COL = 0;                 // pass-1 accumulator: NB columns
+  static constexpr uint32_t D2_COL = 32;               // pass-2 accumulator: 16 columns
   static constexpr uint32_t A_LO = 64;                 // bf16 lo(S): 64 columns of packed pairs
-  static constexpr int NB2 = 16;                       // rows of the pass-2 B operand (bf16 X, zero padded)
+  static constexpr int NB2 = 16;                       // pass-2 N (minimum for M = 128)
+  static constexpr int G2 = (NJ + 7) / 8;              // 8-row groups of bf16(X) that hold data
   static constexpr int SLAB = DIM * 128;               // one 32-column K slab of the tile (bytes)
   static constexpr int TILE = DIM * DIM * 4;
+  static constexpr int B2_SLAB = G2 * 1024;            // one 64-element K slab of the pass-2 operand
+  static constexpr int B2_BYTES = 2 * B2_SLAB;
   static constexpr int B_SLAB = NB * 128;
   static constexpr int B_BYTES = 4 * B_SLAB;
   struct Window {  // per-unit scalars
@@ -70,10 +74,13 @@ struct VerifyTcShape {
     float gpart[4][QT * QT];  // Gram partial sums per K slab
     Window win[2];
   };
-  static constexpr int SMEM = 1024 /* alignment slack */ + TILE + B_BYTES + static_cast<int>(sizeof(Small));
-  static_assert(NB <= static_cast<int>(A_LO) && (NB == 16 || NB == 32), "accumulator columns");
-  static_assert(NJ <= NB2 && 2 * NB2 * 128 <= B_BYTES, "pass-2 B operand reuses the B buffer");
-  static_assert(B_SLAB % 1024 == 0, "B operand slabs must stay 1024-byte aligned");
+  // tile | pass-2 operand | pass-1 operand | scalars; the dynamic shared memory
+  // base is 1024-byte aligned (checked at run time), as the 128-byte swizzle
+  // atoms require
+  static constexpr int SMEM = TILE + B2_BYTES + B_BYTES + static_cast<int>(sizeof(Small));
+  static_assert(NB <= static_cast<int>(D2_COL) && (NB == 16 || NB == 32), "accumulator columns");
+  static_assert(NJ <= NB2, "pass-2 operand rows");
+  static_assert(B_SLAB % 1024 == 0 && B2_SLAB % 1024 == 0, "operand slabs must stay 1024-byte aligned");
 };
 
 template <int QT, typename Act>
@@ -194,12 +201,15 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   using Window = typename Sh::Window;
   constexpr int DIM = Sh::DIM, NJ = Sh::NJ, NB = Sh::NB, EPL = DIM / 32;
   constexpr int PER_WARP = (NJ + 7) / 8;  // q/k vectors staged per warp
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char *smem = reinterpret_cast<unsigned char *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  unsigned char *tile = smem;
-  unsigned char *bop = smem + Sh::TILE;
-  Small &sm = *reinterpret_cast<Small *>(smem + Sh::TILE + Sh::B_BYTES);
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  if ((ptx::smem_addr(smem_raw) & 1023u) != 0) {  // swizzle atoms need 1024-byte alignment
+    if (threadIdx.x == 0) atomicExch(p.status, kStatusMisaligned);
+    return;
+  }
+  unsigned char *tile = smem_raw;
+  unsigned char *b2op = smem_raw + Sh::TILE;  // pass-2 operand: bf16(X)
+  unsigned char *bop = b2op + Sh::B2_BYTES;    // pass-1 operand: [hi(X); lo(X)]
+  Small &sm = *reinterpret_cast<Small *>(bop + Sh::B_BYTES);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -290,7 +300,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   ptx::tc_fence_after_sync();
   const uint32_t tmem = sm.tmem;
   constexpr uint32_t IDESC = ptx::tf32_instr_desc<128, NB>();
-  const uint32_t tile_addr = ptx::smem_addr(tile), b_addr = ptx::smem_addr(bop);
+  const uint32_t tile_addr = ptx::smem_addr(tile), b_addr = ptx::smem_addr(bop), b2_addr = ptx::smem_addr(b2op);
   uint32_t tile_par = 0, mma_par = 0;
   bool ok = true;
 
@@ -398,7 +408,6 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           const uint64_t b = ptx::sw128_kmajor_desc(b_addr + (kk >> 2) * Sh::B_SLAB + sub);
           ptx::mma_tf32(tmem + Sh::D_COL, a, b, IDESC, kk > 0);
         }
-        ptx::mma_commit(&sm.mma_bar);
       }
       // ---- while pass 1 runs: bf16 lo(S) -> tensor memory ---------------------- //
       // warp w: rows 32 (w % 4) .. + 31 (one per lane), K elements 64 (w / 4) .. + 63
@@ -422,19 +431,46 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         ptx::tmem_st32_u(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::A_LO + 32u * kh, packed_lo);
         ptx::tmem_wait_st();
       }
+      // ---- ... the pass-2 operand bf16(X): G2 8-row groups per 64-element slab ---- //
+#pragma unroll
+      for (int c = 0; c < PER_WARP; ++c) {
+        const int j = warp + 8 * c;
+        if (j >= NJ) continue;
+        const __nv_bfloat162 b01 = __floats2bfloat162_rn(xs[c][0], xs[c][1]);
+        const __nv_bfloat162 b23 = __floats2bfloat162_rn(xs[c][2], xs[c][3]);
+        // lane l holds K elements 4l .. 4l + 3: slab l / 16, chunk (l % 16) / 2, half l % 2
+        const int m = lane >> 4, ch = (lane & 15) >> 1;
+        *reinterpret_cast<uint2 *>(b2op + m * Sh::B2_SLAB + j * 128 + ((ch ^ (j & 7)) << 4) + (lane & 1) * 8) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&b01), *reinterpret_cast<const uint32_t *>(&b23));
+      }
+      if constexpr (8 * Sh::G2 > NJ) {  // zero the unused rows of the last data group
+        constexpr int PAD = (8 * Sh::G2 - NJ) * 8;  // 16-byte chunks per slab
+        for (int e = tid; e < 2 * PAD; e += kVerifyThreads) {
+          const int m = e / PAD, rem = e % PAD;
+          *reinterpret_cast<uint4 *>(b2op + m * Sh::B2_SLAB + (NJ + rem / 8) * 128 + ((rem % 8) << 4)) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
       // ---- ... the Gram partial sums and the next units' loads ---------------- //
       if (warp >= 4) gram_partials<QT, NJ, Sh::B_SLAB>(bop, sm.gpart, warp - 4, lane);
       prefetch();
+      ptx::fence_proxy_async_smem();  // pass-2 operand -> tensor-core reads
       ptx::tc_fence_before_sync();
-      if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
-        if (tid == 0) atomicExch(p.status, kStatusMmaTimeout);
-        ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs);
-        ok = false;
-        break;
+      __syncthreads();  // lo(S) in tensor memory, bf16(X) staged, Gram partials written
+      // ---- pass 2 right behind pass 1: bf16 lo(S) x bf16(X) into its own columns -- //
+      // N = 16: rows past the G2 data groups are read from the following bytes of
+      // shared memory (the next slab or the pass-1 operand) and only reach
+      // accumulator columns that are never read.
+      if (tid == 0) {
+        ptx::tc_fence_after_sync();
+        constexpr uint32_t IDESC2 = ptx::bf16_instr_desc<128, Sh::NB2>();
+#pragma unroll
+        for (int kk = 0; kk < DIM / 16; ++kk) {
+          const uint64_t b = ptx::sw128_kmajor_desc(b2_addr + (kk >> 2) * Sh::B2_SLAB + (kk & 3) * 32);
+          ptx::mma_bf16_ts(tmem + Sh::D2_COL, tmem + Sh::A_LO + kk * 8, b, IDESC2, kk > 0);
+        }
+        ptx::mma_commit(&sm.mma_bar);
       }
-      mma_par ^= 1u;
-      // ---- the tile is read (pass 1 and lo(S)): start the next unit's load ---- //
-      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
       // ---- Gram coefficients and decay products of this window ---------------- //
       if (tid < QT * QT) gram_finalize<QT>(sm.gpart, w.dec, w.mkk, w.mkq, tid);
       if (tid == 32) {
@@ -445,43 +481,6 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           w.A[t] = a;
         }
       }
-      // ---- pass 2: bf16 lo(S) x bf16(X), B rewritten in place ----------------- //
-      // B2 (NB2 rows, K-major, 128-byte swizzle, 64 bf16 per row and slab): row j
-      // = bf16(x_j) for j < NJ, zero above (those columns hold hi(S) lo(X)).
-      {
-        constexpr int B2_SLAB = Sh::NB2 * 128;
-#pragma unroll
-        for (int c = 0; c < PER_WARP; ++c) {
-          const int j = warp + 8 * c;
-          if (j >= NJ) continue;
-          const __nv_bfloat162 b01 = __floats2bfloat162_rn(xs[c][0], xs[c][1]);
-          const __nv_bfloat162 b23 = __floats2bfloat162_rn(xs[c][2], xs[c][3]);
-          // lane l holds K elements 4l .. 4l + 3: slab l / 16, chunk (l % 16) / 2, half l % 2
-          const int m = lane >> 4, ch = (lane & 15) >> 1;
-          *reinterpret_cast<uint2 *>(bop + m * B2_SLAB + j * 128 + ((ch ^ (j & 7)) << 4) + (lane & 1) * 8) =
-              make_uint2(*reinterpret_cast<const uint32_t *>(&b01), *reinterpret_cast<const uint32_t *>(&b23));
-        }
-        if constexpr (Sh::NB2 > NJ) {
-          constexpr int PAD = (Sh::NB2 - NJ) * 8;  // 16-byte chunks per slab
-          for (int e = tid; e < 2 * PAD; e += kVerifyThreads) {
-            const int m = e / PAD, rem = e % PAD;
-            *reinterpret_cast<uint4 *>(bop + m * B2_SLAB + (NJ + rem / 8) * 128 + ((rem % 8) << 4)) =
-                make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
-      }
-      ptx::fence_proxy_async_smem();  // B2 -> tensor-core reads
-      __syncthreads();
-      if (tid == 0) {
-        ptx::tc_fence_after_sync();
-        constexpr uint32_t IDESC2 = ptx::bf16_instr_desc<128, Sh::NB2>();
-#pragma unroll
-        for (int kk = 0; kk < DIM / 16; ++kk) {
-          const uint64_t b = ptx::sw128_kmajor_desc(b_addr + (kk >> 2) * (Sh::NB2 * 128) + (kk & 3) * 32);
-          ptx::mma_bf16_ts(tmem + Sh::D_COL, tmem + Sh::A_LO + kk * 8, b, IDESC2, true);
-        }
-        ptx::mma_commit(&sm.mma_bar);
-      }
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
         if (tid == 0) atomicExch(p.status, kStatusMmaTimeout);
         ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs);
@@ -489,11 +488,15 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         break;
       }
       mma_par ^= 1u;
+      // ---- both passes done, the tile is free: start the next unit's load ---- //
+      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
       // ---- per-row recurrence: lane = state row of the warp's lane quadrant --- //
       ptx::tc_fence_after_sync();
-      float d[NB];
+      float d[NB], d2[16];
       __syncwarp();  // tcgen05.ld is warp-wide (.sync.aligned)
-      ptx::tmem_ld_sync<NB>(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::D_COL, d);
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+      ptx::tmem_ld_sync<NB>(lane_base + Sh::D_COL, d);
+      ptx::tmem_ld_sync<16>(lane_base + Sh::D2_COL, d2);
       ptx::tc_fence_before_sync();
       const bool writer_corr = warp < 4;
       float cr[QT];
@@ -501,14 +504,14 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       for (int t = 0; t < QT; ++t) {
         cr[t] = 0.f;
         if (!((vmask >> t) & 1)) continue;
-        float kv = w.A[t] * (d[t] + d[NJ + t]);
+        float kv = w.A[t] * ((d[t] + d[NJ + t]) + d2[t]);
 #pragma unroll
         for (int s2 = 0; s2 < t; ++s2) kv = fmaf(w.mkk[t][s2], cr[s2], kv);
         cr[t] = w.beta[t] * (to_f32<Act>(ic.v[t]) - kv);
         if (writer_corr) {
           if (rec_ok) p.corr[row * p.corr_rs + hv * p.corr_hs + t * p.corr_ts + r] = cr[t];
         } else {
-          float o = w.A[t] * (d[QT + t] + d[NJ + QT + t]);
+          float o = w.A[t] * ((d[QT + t] + d[NJ + QT + t]) + d2[QT + t]);
 #pragma unroll
           for (int s2 = 0; s2 <= t; ++s2) o = fmaf(w.mkq[t][s2], cr[s2], o);
           out[(m0.bos + t) * p.out_ts + hv * DIM + r] = from_f32<Act>(o);
