@@ -6,37 +6,38 @@
 // that product runs on the 5th-generation tensor cores (tcgen05.mma,
 // kind::tf32, M = 128 state rows, accumulators in tensor memory).
 //
-// fp32 accuracy from tf32 operands (three-product split): every operand x is
-// written as x = hi(x) + lo(x) with hi(x) = x with its low 13 mantissa bits
-// cleared (exactly a tf32 value) and lo(x) = x - hi(x) (exact in fp32).  The
-// B operand holds the rows [hi(X); lo(X)] (2 x 2Q rows, padded to a multiple
-// of 16), so one MMA pass over the tile as loaded gives S_hi X_hi and S_hi
-// X_lo side by side in tensor memory (the tensor core reads an fp32 operand
-// as tf32 by dropping the same 13 bits).  The tile is then rewritten in place
-// as lo(S) and a second pass accumulates lo(S) X_hi and lo(S) X_lo into the
-// same columns.  Column j plus column 2Q + j is the dot product with only the
-// lo x lo truncation left out: relative error ~2^-21, the size of fp32
-// rounding over a 128-term sum.
+// fp32 accuracy from tf32 / bf16 operands (split products): every operand x
+// is written as x = hi(x) + lo(x) with hi(x) = x with its low 13 mantissa
+// bits cleared (exactly a tf32 value) and lo(x) = x - hi(x) (exact in fp32).
+//   pass 1 (16 x kind::tf32, A = the TMA-loaded tile, which the tensor core
+//          reads as tf32 by dropping the same 13 bits, i.e. hi(S); B = the
+//          rows [hi(X); lo(X)] padded to a multiple of 16) gives hi(S) hi(X)
+//          and hi(S) lo(X) side by side in tensor memory;
+//   pass 2 (8 x kind::f16, A = bf16(lo(S)) written by the threads into tensor
+//          memory, B = bf16(X)) adds lo(S) X in its own columns.
+// Column j + column 2Q + j of pass 1 plus column j of pass 2 is the row's j-th
+// dot product; the dropped terms are below 2^-19 relative.
 //
-// Grid: up to three CTAs (256 threads) per SM, each walking the units
-// blockIdx.x, blockIdx.x + gridDim.x, ...; per unit:
-//   all:      stage hi/lo(X) into B, g / beta, decay and key records (the
+// Grid: up to three CTAs (256 threads) per SM (two at Q = 8), each walking the
+// units blockIdx.x, blockIdx.x + gridDim.x, ...; per unit:
+//   all:      stage [hi(X); lo(X)], g / beta, decay and key records (the
 //             unit's q/k/v/g/beta were loaded into registers during the
-//             previous unit) while the tile is in flight;
-//   thread 0: MMA pass 1 -> commit; meanwhile all threads compute the Gram
-//             coefficients and start the loads of the next units' slots and
-//             activations;
-//   all:      rewrite the tile as lo(S); thread 0: MMA pass 2 -> commit, then
-//             at once the TMA of the NEXT unit's tile (4-D tensor map,
-//             128-byte swizzle: the layout the MMA's K-major descriptor reads
-//             directly, one 128-row box per K slab) into the freed buffer;
-//   all:      every warp loads its 32 rows' sums from tensor memory (one row
-//             per lane) and runs the recurrence -- warps 0-3 write the
-//             correction records, warps 4-7 the outputs -- while that load
-//             is in flight.
-// The per-unit scalars are double-buffered by unit parity.  Every wait is
-// bounded (1 s) and reported through the status word; tensor memory is
-// released on every path after it was allocated.
+//             previous unit); wait for the tile;
+//   thread 0: pass 1, no commit yet;
+//   all:      meanwhile bf16(lo(S)) -> tensor memory (one row per lane),
+//             bf16(X) -> the pass-2 operand, the Gram partial sums, the loads
+//             of the next units' slots and activations;
+//   thread 0: pass 2 right behind pass 1, one commit for both;
+//   all:      Gram coefficients; after the commit, thread 0 starts the NEXT
+//             unit's tile (4-D tensor map, 128-byte swizzle -- the layout
+//             the MMA's K-major descriptor reads directly -- one 128-row box
+//             per K slab) into the freed buffer, and every warp loads its 32
+//             rows' sums from tensor memory (one row per lane) and runs the
+//             recurrence -- warps 0-3 write the correction records, warps
+//             4-7 the outputs -- while that load is in flight.
+// Three CTA barriers per unit; the per-unit scalars are double-buffered by
+// unit parity.  Every wait is bounded (1 s) and reported through the status
+// word; tensor memory is released on every path after it was allocated.
 #pragma once
 
 #include "verify.cuh"
