@@ -15,6 +15,7 @@ from .kernels import (
     GDNRecoverSSMCommitContext,
     ReplayRecordBuffers,
     gdn_recoverssm_verify,
+    gdn_recoverssm_verify_gated,
     record_geometry_bytes,
     record_nbytes,
 )
@@ -28,6 +29,7 @@ __all__ = [
     "NULL_BLOCK_ID",
     "ReplayRecordBuffers",
     "gdn_recoverssm_verify",
+    "gdn_recoverssm_verify_gated",
     "record_geometry_bytes",
     "record_nbytes",
 ]

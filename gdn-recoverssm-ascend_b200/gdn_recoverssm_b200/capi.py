@@ -64,6 +64,10 @@ PROTOTYPES = {
         c_int32,
         [c_void_p] * 12 + [POINTER(c_int64), c_int64, c_float] + [c_int32] * 8 + [c_uint32, c_void_p],
     ),
+    "gdn_rssm_verify_gated": (
+        c_int32,
+        [c_void_p] * 14 + [POINTER(c_int64), c_int64] + [c_float] * 3 + [c_int32] * 9 + [c_uint32, c_void_p],
+    ),
     "gdn_rssm_fold": (
         c_int32,
         [c_void_p] * 9 + [IndexView] + [c_void_p] * 4 + [c_int64, POINTER(c_int64), c_int64] + [c_int32] * 4
@@ -158,6 +162,26 @@ def verify(q, k, v, g, beta, state, correction, key, decay, out, qsl, indices, c
         q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), state.data_ptr(), corr_ptr,
         key_ptr, decay_ptr, out.data_ptr(), qsl.data_ptr(), indices.data_ptr(), cfg, len(config), float(scale),
         _DTYPE[q.dtype], _DTYPE[state.dtype], _DTYPE[beta.dtype], F32 if packed else _DTYPE[key.dtype],
+        _DTYPE[qsl.dtype], _DTYPE[indices.dtype], K, V, flags,
+        current_stream_handle() if stream is None else stream,
+    )
+    check(rc)
+
+
+def verify_gated(q, k, v, a, b, A_log, dt_bias, state, correction, key, decay, out, qsl, indices, config, scale,
+                 softplus_beta, softplus_threshold, *, flags, stream=None):
+    """Call ``gdn_rssm_verify_gated`` with torch tensors' raw device pointers."""
+    K, V = q.shape[-1], v.shape[-1]
+    packed = bool(flags & RECORD_PACKED)
+    cfg = int64_array(config)
+    corr_ptr = correction.data_ptr()
+    key_ptr = corr_ptr + 4 * V if packed else key.data_ptr()
+    decay_ptr = corr_ptr + 4 * (V + K) if packed else decay.data_ptr()
+    rc = lib().gdn_rssm_verify_gated(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(), A_log.data_ptr(), dt_bias.data_ptr(),
+        state.data_ptr(), corr_ptr, key_ptr, decay_ptr, out.data_ptr(), qsl.data_ptr(), indices.data_ptr(), cfg,
+        len(config), float(scale), float(softplus_beta), float(softplus_threshold), _DTYPE[q.dtype],
+        _DTYPE[state.dtype], _DTYPE[a.dtype], _DTYPE[b.dtype], F32 if packed else _DTYPE[key.dtype],
         _DTYPE[qsl.dtype], _DTYPE[indices.dtype], K, V, flags,
         current_stream_handle() if stream is None else stream,
     )

@@ -114,11 +114,14 @@ int gdn_rssm_device_status(int32_t *status, void *stream) {
   return GDN_RSSM_OK;
 }
 
-int gdn_rssm_verify(const void *q, const void *k, const void *v, const float *g, const void *beta, const void *state,
-                    float *correction, void *key, float *decay, void *out, const void *qsl, const void *indices,
-                    const int64_t *config, int64_t config_len, float scale, int32_t activation_dtype,
-                    int32_t state_dtype, int32_t beta_dtype, int32_t key_dtype, int32_t qsl_dtype,
-                    int32_t index_dtype, int32_t key_dim, int32_t value_dim, uint32_t flags, void *stream) {
+static int verify_impl(const void *q, const void *k, const void *v, const void *g, const void *beta,
+                       const void *state, float *correction, void *key, float *decay, void *out, const void *qsl,
+                       const void *indices, const int64_t *config, int64_t config_len, float scale,
+                       int32_t activation_dtype, int32_t state_dtype, int32_t gate_dtype, int32_t beta_dtype,
+                       int32_t key_dtype, int32_t qsl_dtype, int32_t index_dtype, int32_t key_dim, int32_t value_dim,
+                       uint32_t flags, const float *A_log, const float *dt_bias, float softplus_beta,
+                       float softplus_threshold, void *stream) {
+  const bool gated = A_log != nullptr;
   GDN_REQUIRE(config != nullptr && config_len == GDN_RSSM_VERIFY_FIELDS, "verify config must have 28 fields");
   int64_t f[GDN_RSSM_VERIFY_FIELDS];
   std::memcpy(f, config, sizeof(f));
@@ -164,6 +167,11 @@ int gdn_rssm_verify(const void *q, const void *k, const void *v, const float *g,
   GDN_REQUIRE(state_dtype == GDN_RSSM_F32 || (state_dtype == GDN_RSSM_BF16 && key_dim >= 64),
               "state must be FP32 (or BF16 with K >= 64)");
   GDN_REQUIRE(beta_dtype == GDN_RSSM_F32 || beta_dtype == activation_dtype, "beta must be FP32 or the activation dtype");
+  GDN_REQUIRE(gate_dtype == GDN_RSSM_F32 || (gated && gate_dtype == activation_dtype),
+              "the gate must be FP32 (or, raw, the activation dtype)");
+  if (gated) {
+    GDN_REQUIRE(dt_bias != nullptr && softplus_beta > 0.f, "gating needs A_log, dt_bias and softplus_beta > 0");
+  }
   if (packed) {
     GDN_REQUIRE(key_dtype == GDN_RSSM_F32, "packed records must remain FP32");
   } else {
@@ -191,6 +199,11 @@ int gdn_rssm_verify(const void *q, const void *k, const void *v, const float *g,
   p.v = v;
   p.g = g;
   p.beta = beta;
+  p.A_log = A_log;
+  p.dt_bias = dt_bias;
+  p.softplus_beta = softplus_beta;
+  p.softplus_threshold = softplus_threshold;
+  p.gate_dtype = gate_dtype;
   p.corr = correction;
   p.key = key;
   p.decay = decay;
@@ -202,7 +215,7 @@ int gdn_rssm_verify(const void *q, const void *k, const void *v, const float *g,
   p.key_dtype = key_dtype;
   p.qsl_dtype = qsl_dtype;
   p.index_dtype = index_dtype;
-  p.flags = flags;
+  p.flags = flags | (gated ? kGateInKernel : 0u);
   L.state = state;
   L.state_dtype = state_dtype;
   L.dim = key_dim;
@@ -212,6 +225,29 @@ int gdn_rssm_verify(const void *q, const void *k, const void *v, const float *g,
     case GDN_RSSM_F16: return launch_verify_f16(L);
     default: return launch_verify_f32(L);
   }
+}
+
+int gdn_rssm_verify(const void *q, const void *k, const void *v, const float *g, const void *beta, const void *state,
+                    float *correction, void *key, float *decay, void *out, const void *qsl, const void *indices,
+                    const int64_t *config, int64_t config_len, float scale, int32_t activation_dtype,
+                    int32_t state_dtype, int32_t beta_dtype, int32_t key_dtype, int32_t qsl_dtype,
+                    int32_t index_dtype, int32_t key_dim, int32_t value_dim, uint32_t flags, void *stream) {
+  return verify_impl(q, k, v, g, beta, state, correction, key, decay, out, qsl, indices, config, config_len, scale,
+                     activation_dtype, state_dtype, GDN_RSSM_F32, beta_dtype, key_dtype, qsl_dtype, index_dtype,
+                     key_dim, value_dim, flags, nullptr, nullptr, 0.f, 0.f, stream);
+}
+
+int gdn_rssm_verify_gated(const void *q, const void *k, const void *v, const void *a, const void *b, const float *A_log,
+                          const float *dt_bias, const void *state, float *correction, void *key, float *decay,
+                          void *out, const void *qsl, const void *indices, const int64_t *config, int64_t config_len,
+                          float scale, float softplus_beta, float softplus_threshold, int32_t activation_dtype,
+                          int32_t state_dtype, int32_t gate_dtype, int32_t b_dtype, int32_t key_dtype,
+                          int32_t qsl_dtype, int32_t index_dtype, int32_t key_dim, int32_t value_dim, uint32_t flags,
+                          void *stream) {
+  GDN_REQUIRE(A_log != nullptr, "gdn_rssm_verify_gated needs A_log");
+  return verify_impl(q, k, v, a, b, state, correction, key, decay, out, qsl, indices, config, config_len, scale,
+                     activation_dtype, state_dtype, gate_dtype, b_dtype, key_dtype, qsl_dtype, index_dtype, key_dim,
+                     value_dim, flags, A_log, dt_bias, softplus_beta, softplus_threshold, stream);
 }
 
 int gdn_rssm_fold(const int64_t *state_addrs, const int64_t *state_block_strides, const int64_t *corr_addrs,

@@ -81,10 +81,17 @@ void check_table(const Tensor &t, const Tensor &ref, int64_t layers, at::ScalarT
 
 // verify with explicit flags: packed records (correction == key == decay ==
 // the packed fp32 record tensor) and/or in-kernel q/k normalisation.
-void verify_ext(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor &g, const Tensor &beta,
-                const Tensor &state, const Tensor &correction, const Tensor &key, const Tensor &decay,
-                const Tensor &out, const Tensor &qsl, const Tensor &indices, at::IntArrayRef config, double scale,
-                int64_t flags) {
+// Gate inputs of verify_gated_ext: g / beta slots carry the raw a / b.
+struct GateArgs {
+  const Tensor &A_log;
+  const Tensor &dt_bias;
+  double softplus_beta, softplus_threshold;
+};
+
+void verify_common(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor &g, const Tensor &beta,
+                   const Tensor &state, const Tensor &correction, const Tensor &key, const Tensor &decay,
+                   const Tensor &out, const Tensor &qsl, const Tensor &indices, at::IntArrayRef config, double scale,
+                   int64_t flags, const GateArgs *gate) {
   TORCH_CHECK(config.size() == GDN_RSSM_VERIFY_FIELDS, "GDN RecoverSSM: verify config must have 28 fields");
   TORCH_CHECK(q.is_cuda(), "GDN RecoverSSM: verify requires CUDA tensors");
   for (auto *t : {&k, &v, &g, &beta, &state, &correction, &key, &decay, &out, &qsl, &indices}) same_cuda(*t, q, "input");
@@ -97,9 +104,16 @@ void verify_ext(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor 
   TORCH_CHECK(q.stride(3) == 1 && q.stride(2) == q.size(3) && k.stride(3) == 1 && k.stride(2) == k.size(3) &&
                   v.stride(3) == 1 && v.stride(2) == v.size(3) && out.stride(3) == 1 && out.stride(2) == out.size(3),
               "GDN RecoverSSM: q/k/v/out heads must be contiguous");
-  TORCH_CHECK(g.scalar_type() == at::kFloat && correction.scalar_type() == at::kFloat &&
-                  decay.scalar_type() == at::kFloat,
+  TORCH_CHECK((g.scalar_type() == at::kFloat || (gate && g.scalar_type() == q.scalar_type())) &&
+                  correction.scalar_type() == at::kFloat && decay.scalar_type() == at::kFloat,
               "GDN RecoverSSM: FP32 gate/correction/decay required");
+  if (gate) {
+    for (const Tensor *t : {&gate->A_log, &gate->dt_bias}) {
+      same_cuda(*t, q, "A_log / dt_bias");
+      TORCH_CHECK(t->dim() == 1 && t->size(0) == v.size(2) && t->stride(0) == 1 && t->scalar_type() == at::kFloat,
+                  "GDN RecoverSSM: A_log and dt_bias must be contiguous FP32 [value heads]");
+    }
+  }
   TORCH_CHECK(g.dim() == 2 && beta.dim() == 2 && g.stride(1) == 1 && beta.stride(1) == 1,
               "GDN RecoverSSM: gate and beta must be [tokens, value heads] with contiguous heads");
   TORCH_CHECK(state.dim() == 4 && state.stride(3) == 1, "GDN RecoverSSM: state must be [blocks, HV, V, K]");
@@ -134,13 +148,43 @@ void verify_ext(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor 
   const c10::cuda::CUDAGuard guard(q.device());
   const auto stream = at::cuda::getCurrentCUDAStream(q.get_device()).stream();
   std::vector<int64_t> cfg(config.begin(), config.end());
-  check_rc(gdn_rssm_verify(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), beta.data_ptr(),
-                           state.data_ptr(), corr_ptr, key_ptr, decay_ptr, out.data_ptr(), qsl.data_ptr(),
-                           indices.data_ptr(), cfg.data(), static_cast<int64_t>(cfg.size()), static_cast<float>(scale),
-                           code_of(q.scalar_type()), code_of(state.scalar_type()), code_of(beta.scalar_type()),
-                           packed ? GDN_RSSM_F32 : code_of(key.scalar_type()), code_of(qsl.scalar_type()),
-                           code_of(indices.scalar_type()), static_cast<int32_t>(K), static_cast<int32_t>(V),
-                           static_cast<uint32_t>(flags), stream));
+  const int32_t key_code = packed ? GDN_RSSM_F32 : code_of(key.scalar_type());
+  if (gate == nullptr) {
+    check_rc(gdn_rssm_verify(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), beta.data_ptr(),
+                             state.data_ptr(), corr_ptr, key_ptr, decay_ptr, out.data_ptr(), qsl.data_ptr(),
+                             indices.data_ptr(), cfg.data(), static_cast<int64_t>(cfg.size()),
+                             static_cast<float>(scale), code_of(q.scalar_type()), code_of(state.scalar_type()),
+                             code_of(beta.scalar_type()), key_code, code_of(qsl.scalar_type()),
+                             code_of(indices.scalar_type()), static_cast<int32_t>(K), static_cast<int32_t>(V),
+                             static_cast<uint32_t>(flags), stream));
+  } else {
+    check_rc(gdn_rssm_verify_gated(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), gate->A_log.data_ptr<float>(),
+        gate->dt_bias.data_ptr<float>(), state.data_ptr(), corr_ptr, key_ptr, decay_ptr, out.data_ptr(),
+        qsl.data_ptr(), indices.data_ptr(), cfg.data(), static_cast<int64_t>(cfg.size()), static_cast<float>(scale),
+        static_cast<float>(gate->softplus_beta), static_cast<float>(gate->softplus_threshold),
+        code_of(q.scalar_type()), code_of(state.scalar_type()), code_of(g.scalar_type()), code_of(beta.scalar_type()),
+        key_code, code_of(qsl.scalar_type()), code_of(indices.scalar_type()), static_cast<int32_t>(K),
+        static_cast<int32_t>(V), static_cast<uint32_t>(flags), stream));
+  }
+}
+
+void verify_ext(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor &g, const Tensor &beta,
+                const Tensor &state, const Tensor &correction, const Tensor &key, const Tensor &decay,
+                const Tensor &out, const Tensor &qsl, const Tensor &indices, at::IntArrayRef config, double scale,
+                int64_t flags) {
+  verify_common(q, k, v, g, beta, state, correction, key, decay, out, qsl, indices, config, scale, flags, nullptr);
+}
+
+// verify with the gates computed in the kernel from the raw inputs a, b and
+// the per-head A_log, dt_bias (the upstream fused form).
+void verify_gated_ext(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor &a, const Tensor &b,
+                      const Tensor &A_log, const Tensor &dt_bias, const Tensor &state, const Tensor &correction,
+                      const Tensor &key, const Tensor &decay, const Tensor &out, const Tensor &qsl,
+                      const Tensor &indices, at::IntArrayRef config, double scale, double softplus_beta,
+                      double softplus_threshold, int64_t flags) {
+  const GateArgs gate{A_log, dt_bias, softplus_beta, softplus_threshold};
+  verify_common(q, k, v, a, b, state, correction, key, decay, out, qsl, indices, config, scale, flags, &gate);
 }
 
 // The reference schema: typed records, q/k already normalised.
@@ -351,6 +395,10 @@ TORCH_LIBRARY(gdn_recoverssm_ac, m) {
       "Tensor(b!) key, Tensor(c!) decay, Tensor(d!) out, Tensor qsl, Tensor indices, int[] config, float scale, "
       "int flags) -> ()");
   m.def(
+      "verify_gated_ext(Tensor q, Tensor k, Tensor v, Tensor a, Tensor b, Tensor A_log, Tensor dt_bias, "
+      "Tensor state, Tensor(a!) correction, Tensor(b!) key, Tensor(c!) decay, Tensor(d!) out, Tensor qsl, "
+      "Tensor indices, int[] config, float scale, float softplus_beta, float softplus_threshold, int flags) -> ()");
+  m.def(
       "fold_ext(Tensor(a!) state, Tensor correction, Tensor key, Tensor decay, Tensor state_addrs, "
       "Tensor state_block_strides, Tensor corr_addrs, Tensor corr_block_strides, Tensor key_addrs, "
       "Tensor key_block_strides, Tensor decay_addrs, Tensor decay_block_strides, Tensor layer_groups, "
@@ -383,6 +431,7 @@ TORCH_LIBRARY_IMPL(gdn_recoverssm_ac, CUDA, m) {
   m.impl("verify", TORCH_FN(verify));
   m.impl("fold", TORCH_FN(fold));
   m.impl("verify_ext", TORCH_FN(verify_ext));
+  m.impl("verify_gated_ext", TORCH_FN(verify_gated_ext));
   m.impl("fold_ext", TORCH_FN(fold_ext));
   m.impl("commit_plan", TORCH_FN(commit_plan));
   m.impl("grouped_plan", TORCH_FN(grouped_plan));
@@ -398,6 +447,10 @@ TORCH_LIBRARY_IMPL(gdn_recoverssm_ac, Meta, m) {
   m.impl("verify_ext", [](const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &,
                           const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &,
                           const Tensor &, const Tensor &, at::IntArrayRef, double, int64_t) {});
+  m.impl("verify_gated_ext", [](const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &,
+                                const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &,
+                                const Tensor &, const Tensor &, const Tensor &, const Tensor &, at::IntArrayRef,
+                                double, double, double, int64_t) {});
   m.impl("fold", [](const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &,
                     const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &,
                     const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &, const Tensor &,

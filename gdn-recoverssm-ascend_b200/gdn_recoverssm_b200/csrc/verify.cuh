@@ -1,4 +1,5 @@
-// Speculative verify kernel (sm_100a): persistent, warp-specialised pipeline.
+// Speculative verify kernel (sm_100a), CUDA-core form: K = V in {32, 64}, or
+// a bf16 state pool (K = V = 128 with an fp32 pool runs verify_tc.cuh).
 //
 // Semantics follow the reference verify (kernels.py:491-697; AscendC
 // verify.h:350-398): per (sequence row, value head) "unit", read the fp32
@@ -43,8 +44,10 @@ namespace gdn_rssm {
 
 struct VerifyParams {
   const void *q, *k, *v;
-  const float *g;
-  const void *beta;
+  const void *g;     // log-space decay g, or the raw gate input a (kGateInKernel)
+  const void *beta;  // beta, or the raw input b (kGateInKernel)
+  const float *A_log, *dt_bias;  // [HV] (kGateInKernel)
+  float softplus_beta, softplus_threshold;
   float *corr;
   void *key;
   float *decay;
@@ -58,9 +61,31 @@ struct VerifyParams {
   int64_t decay_rs, decay_hs, decay_ts;
   int64_t out_ts, qsl_stride, index_stride;
   float scale;
-  int32_t beta_dtype, key_dtype, qsl_dtype, index_dtype;
+  int32_t gate_dtype, beta_dtype, key_dtype, qsl_dtype, index_dtype;
   uint32_t flags;
 };
+
+// Internal flag (set by gdn_rssm_verify_gated): the g / beta slots hold the
+// raw gate inputs a / b, and the kernel computes the gates.
+constexpr uint32_t kGateInKernel = 1u << 8;
+
+// Decay exp(g) and beta of value head hv from the two values loaded from the
+// g and beta slots.  Gated: g = -exp(A_log) * softplus(a + dt_bias) with
+// softplus(x) = log1p(exp(sb x)) / sb below the threshold and x above it,
+// beta = sigmoid(b).
+__device__ __forceinline__ void token_gates(const VerifyParams &p, int hv, float graw, float braw, float &dec,
+                                            float &bet) {
+  if (p.flags & kGateInKernel) {
+    const float x = graw + p.dt_bias[hv];
+    const float bx = p.softplus_beta * x;
+    const float sp = bx <= p.softplus_threshold ? log1pf(expf(bx)) / p.softplus_beta : x;
+    dec = expf(-expf(p.A_log[hv]) * sp);
+    bet = 1.f / (1.f + expf(-braw));
+  } else {
+    dec = expf(graw);
+    bet = braw;
+  }
+}
 
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
@@ -260,10 +285,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
       vv[c] = (i < QT * DIM && ((valid_mask >> t) & 1)) ? vin[(bos + t) * p.v_ts + hv * DIM + e] : from_f32<Act>(0.f);
     }
     float dec = 1.f, bet = 0.f;
-    if (tid < QT && ((valid_mask >> tid) & 1)) {
-      dec = expf(p.g[(bos + tid) * p.g_ts + hv]);
-      bet = load_float(p.beta, (bos + tid) * p.beta_ts + hv, p.beta_dtype);
-    }
+    if (tid < QT && ((valid_mask >> tid) & 1))
+      token_gates(p, hv, load_float(p.g, (bos + tid) * p.g_ts + hv, p.gate_dtype),
+                  load_float(p.beta, (bos + tid) * p.beta_ts + hv, p.beta_dtype), dec, bet);
 #pragma unroll
     for (int c = 0; c < VPER; ++c) {
       const int i = tid + c * kVerifyThreads;

@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     in.g = 0.f;
     in.beta = 0.f;
     if (tid < QT && ((vmask >> tid) & 1)) {
-      in.g = p.g[(m.bos + tid) * p.g_ts + hv];
+      in.g = load_float(p.g, (m.bos + tid) * p.g_ts + hv, p.gate_dtype);
       in.beta = load_float(p.beta, (m.bos + tid) * p.beta_ts + hv, p.beta_dtype);
     }
   };
@@ -333,9 +333,10 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       // ---- stage the window --------------------------------------------------- //
       if (tid < QT) {
         const bool live = (vmask >> tid) & 1;
-        const float dec = live ? expf(ic.g) : 1.f;
+        float dec = 1.f, bet = 0.f;
+        if (live) token_gates(p, hv, ic.g, ic.beta, dec, bet);
         w.dec[tid] = dec;
-        w.beta[tid] = live ? ic.beta : 0.f;
+        w.beta[tid] = bet;
         if (rec_ok && live) p.decay[row * p.decay_rs + hv * p.decay_hs + tid * p.decay_ts] = dec;
       }
       if constexpr (NB > 2 * NJ) {  // zero padding rows of B (Q < 4)

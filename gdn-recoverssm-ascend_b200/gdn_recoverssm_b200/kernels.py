@@ -10,6 +10,8 @@ between backends and no CPU fallback: CPU tensors are rejected by the ops.
 
 Public entry points (reference line numbers):
   * ``gdn_recoverssm_verify``                 kernels.py:700-928
+  * ``gdn_recoverssm_verify_gated``           gates fused into the prologue,
+    argument names of docs/reference/recoverssm_gdn_upstream.py:175-330
   * ``ReplayRecordBuffers``                   kernels.py:166-247
   * ``record_nbytes`` / ``record_geometry_bytes`` kernels.py:250-294
   * ``GDNRecoverSSMCommitContext.from_tensors`` kernels.py:1421-1565
@@ -182,6 +184,59 @@ def gdn_recoverssm_verify(
     q/k inside the kernel (``x * rsqrt(sum(x^2) + 1e-6)``).  Returns ``out``
     ``[1, T, HV, V]``.  Launches on the current CUDA stream.
     """
+    return _verify(g, beta, q, k, v, checkpoint_state, replay_cache, query_start_loc, state_indices, spec_query_len,
+                   scale, qk_already_normalized, out, _collect, None)
+
+
+def gdn_recoverssm_verify_gated(
+    A_log: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    dt_bias: torch.Tensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    checkpoint_state: torch.Tensor,
+    replay_cache,
+    query_start_loc: torch.Tensor,
+    state_indices: torch.Tensor,
+    spec_query_len: int,
+    scale: float | None = None,
+    softplus_beta: float = 1.0,
+    softplus_threshold: float = 20.0,
+    use_qk_l2norm_in_kernel: bool = True,
+    out: torch.Tensor | None = None,
+    _collect: list | None = None,
+) -> torch.Tensor:
+    """Verify with the gates computed in the kernel prologue from the raw
+    model inputs (the fused-gating form of
+    ``docs/reference/recoverssm_gdn_upstream.py:175-330``, kernel math :111-150):
+    per token and value head ``g = -exp(A_log[h]) * softplus(a + dt_bias[h])``
+    with ``softplus(x) = log(1 + exp(sb*x)) / sb`` while ``sb*x <= threshold``
+    (``x`` above it), ``decay = exp(g)`` and ``beta = sigmoid(b)``.
+
+    ``a``, ``b`` are ``[T, HV]`` or ``[1, T, HV]`` in FP32 or the activation
+    dtype; ``A_log`` and ``dt_bias`` are FP32 ``[HV]``.  Everything else (and
+    the records, indexed by request row as in ``gdn_recoverssm_verify``) is
+    exactly ``gdn_recoverssm_verify``; ``use_qk_l2norm_in_kernel=True``
+    normalises q/k in the kernel.
+    """
+    HV = v.shape[-2] if v.ndim == 4 else -1
+    _require(tuple(A_log.shape) == (HV,) and tuple(dt_bias.shape) == (HV,), "A_log or dt_bias shape is incompatible")
+    _require(A_log.dtype == torch.float32 and dt_bias.dtype == torch.float32, "A_log and dt_bias must be FP32")
+    _require(A_log.device == q.device and dt_bias.device == q.device, "inputs must be on the same device")
+    _require(softplus_beta > 0, "softplus_beta must be positive")
+    gate = (A_log.contiguous(), dt_bias.contiguous(), float(softplus_beta), float(softplus_threshold))
+    return _verify(a, b, q, k, v, checkpoint_state, replay_cache, query_start_loc, state_indices, spec_query_len,
+                   scale, not use_qk_l2norm_in_kernel, out, _collect, gate)
+
+
+def _verify(g, beta, q, k, v, checkpoint_state, replay_cache, query_start_loc, state_indices, spec_query_len, scale,
+            qk_already_normalized, out, _collect, gate):
+    """Shared validation and launch of both verify forms; ``gate`` is
+    ``(A_log, dt_bias, softplus_beta, softplus_threshold)`` for the fused
+    gating form (``g`` / ``beta`` then carry the raw ``a`` / ``b``)."""
     _require(q.ndim == 4 and q.shape[0] == 1, "q must have shape [1, tokens, heads, dim]")
     _, total, H, K = q.shape
     _require(k.shape == q.shape, "q and k shapes differ")
@@ -199,7 +254,10 @@ def gdn_recoverssm_verify(
     nb = checkpoint_state.shape[0]
     _require(tuple(checkpoint_state.shape[1:]) == (HV, V, K), "checkpoint shape is incompatible")
     _require(K == V and K in SUPPORTED_HEAD_DIMS, f"K and V must be equal and one of {SUPPORTED_HEAD_DIMS}")
-    _require(g2.dtype == torch.float32, "gate must be FP32 log-space decay")
+    if gate is None:
+        _require(g2.dtype == torch.float32, "gate must be FP32 log-space decay")
+    else:
+        _require(g2.dtype in (torch.float32, q.dtype), "a must be FP32 or the activation dtype")
     _require(beta2.dtype in (torch.float32, q.dtype), "beta must be FP32 or the activation dtype")
     _require(q.dtype in (torch.float32, torch.bfloat16, torch.float16) and k.dtype == q.dtype and v.dtype == q.dtype,
              "q/k/v must share one FP32/BF16/FP16 dtype")
@@ -265,12 +323,21 @@ def gdn_recoverssm_verify(
         out.stride(1), query_start_loc.stride(0), state_indices.stride(0),
     ]
     flags = (0 if soa else _RECORD_PACKED) | (0 if qk_already_normalized else _NORMALIZE_QK)
-    spec = _LaunchSpec(
-        "verify",
-        _native.ops().verify_ext,
-        (q, k, v, g2, beta2, checkpoint_state, corr, key_record, decay_record, out, query_start_loc,
-         state_indices, config, float(scale), flags),
-    )
+    if gate is None:
+        spec = _LaunchSpec(
+            "verify",
+            _native.ops().verify_ext,
+            (q, k, v, g2, beta2, checkpoint_state, corr, key_record, decay_record, out, query_start_loc,
+             state_indices, config, float(scale), flags),
+        )
+    else:
+        A_log, dt_bias, sb, thr = gate
+        spec = _LaunchSpec(
+            "verify_gated",
+            _native.ops().verify_gated_ext,
+            (q, k, v, g2, beta2, A_log, dt_bias, checkpoint_state, corr, key_record, decay_record, out,
+             query_start_loc, state_indices, config, float(scale), sb, thr, flags),
+        )
     if _collect is None:
         spec.launch()
     else:

@@ -31,6 +31,9 @@
  *   gdn_rssm_compact_conv  <- Triton _grouped_compact_conv_state_kernel
  *                             (grouped_commit.py:225-322) and
  *                             _compact_conv_state_kernel (kernels.py:1075-1169)
+ *   gdn_rssm_verify_gated  <- the gating op in front of verify, fused as in
+ *                             the upstream verify
+ *                             (docs/reference/recoverssm_gdn_upstream.py:39-175)
  */
 #ifndef GDN_RECOVERSSM_B200_H
 #define GDN_RECOVERSSM_B200_H
@@ -158,6 +161,30 @@ GDN_RSSM_API int gdn_rssm_verify(const void *q, const void *k, const void *v, co
                     int32_t state_dtype, int32_t beta_dtype, int32_t key_dtype,
                     int32_t qsl_dtype, int32_t index_dtype, int32_t key_dim,
                     int32_t value_dim, uint32_t flags, void *stream);
+
+/* Verify with the gates computed in the kernel prologue.  Replaces the
+ * separate gating op in front of verify: the reference plugin's upstream
+ * verify (docs/reference/recoverssm_gdn_upstream.py:39-175, host wrapper
+ * :178-330) fuses it the same way; its own torch op has no counterpart.
+ * Same as gdn_rssm_verify except that the raw gate inputs replace g and beta:
+ * a [T,HV] (dtype gate_dtype, token stride = config field g_token_stride),
+ * b [T,HV] (dtype b_dtype, stride = beta_token_stride), A_log [HV] and
+ * dt_bias [HV] fp32, and per token and value head
+ *   g    = -exp(A_log) * softplus(a + dt_bias),
+ *   softplus(x) = log(1 + exp(sb * x)) / sb  if sb * x <= threshold, else x,
+ *   beta = sigmoid(b),
+ * with sb = softplus_beta, threshold = softplus_threshold (the upstream
+ * defaults are 1 and 20).  The decay record is exp(g) as multiplied. */
+GDN_RSSM_API int gdn_rssm_verify_gated(const void *q, const void *k, const void *v, const void *a,
+                    const void *b, const float *A_log, const float *dt_bias,
+                    const void *state, float *correction, void *key, float *decay,
+                    void *out, const void *qsl, const void *indices,
+                    const int64_t *config, int64_t config_len, float scale,
+                    float softplus_beta, float softplus_threshold,
+                    int32_t activation_dtype, int32_t state_dtype, int32_t gate_dtype,
+                    int32_t b_dtype, int32_t key_dtype, int32_t qsl_dtype,
+                    int32_t index_dtype, int32_t key_dim, int32_t value_dim,
+                    uint32_t flags, void *stream);
 
 /* Multi-layer accepted-prefix fold.  Per layer l: state_addrs[l] is the
  * layer's state pool base, state_block_strides[l] its page stride (elements);

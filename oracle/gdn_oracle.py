@@ -25,15 +25,24 @@ MAX_SPEC_QUERY_LEN = 8  # kernels.py:101
 # --------------------------------------------------------------------------- #
 # per-unit math (plugin/tests/test_math_oracle.py)
 # --------------------------------------------------------------------------- #
-def softplus(x):
-    """Overflow-safe softplus (test_math_oracle.py:25-26)."""
+def softplus(x, beta=1.0, threshold=20.0):
+    """Overflow-safe softplus (test_math_oracle.py:25-26); ``beta`` and
+    ``threshold`` as in docs/reference/recoverssm_gdn_upstream.py:141-145
+    (``log(1 + exp(beta*x)) / beta`` while ``beta*x <= threshold``, else x)."""
     x = np.asarray(x, dtype=np.float64)
-    return np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0))))
+    bx = beta * x
+    return np.where(bx > threshold, x, np.log1p(np.exp(np.minimum(bx, threshold))) / beta)
 
 
-def gdn_gate(a_log, dt_bias, a):
-    """Log-space decay ``g = -exp(A_log) * softplus(a + dt_bias)`` (test_math_oracle.py:29-31)."""
-    return -np.exp(a_log) * softplus(np.asarray(a, np.float64) + dt_bias)
+def gdn_gate(a_log, dt_bias, a, beta=1.0, threshold=20.0):
+    """Log-space decay ``g = -exp(A_log) * softplus(a + dt_bias)`` (test_math_oracle.py:29-31;
+    upstream verify prologue docs/reference/recoverssm_gdn_upstream.py:111-146)."""
+    return -np.exp(a_log) * softplus(np.asarray(a, np.float64) + dt_bias, beta, threshold)
+
+
+def sigmoid(b):
+    """``beta = sigmoid(b)`` of the upstream prologue (recoverssm_gdn_upstream.py:147-151)."""
+    return 1.0 / (1.0 + np.exp(-np.asarray(b, np.float64)))
 
 
 def l2_unit(x):

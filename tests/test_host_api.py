@@ -22,7 +22,7 @@ def test_library_exports_every_declared_symbol():
     from gdn_recoverssm_b200 import capi
 
     names = _declared()
-    assert len(names) == 9, names
+    assert len(names) == 10, names
     lib = capi.lib()
     for name in names:
         assert hasattr(lib, name), name
@@ -45,6 +45,11 @@ def test_torch_ops_register_reference_schemas():
     )
     assert fold.startswith("gdn_recoverssm_ac::fold(Tensor(a!) state, Tensor correction, Tensor key, Tensor decay,")
     assert fold.endswith("Tensor boundary_lengths, int[] config) -> ()")
+    # the fused-gating form: upstream argument order for the gate inputs
+    gated = str(ops.verify_gated_ext.default._schema)
+    assert gated.startswith("gdn_recoverssm_ac::verify_gated_ext(Tensor q, Tensor k, Tensor v, Tensor a, Tensor b, "
+                            "Tensor A_log, Tensor dt_bias, Tensor state, Tensor(a!) correction,")
+    assert gated.endswith("float scale, float softplus_beta, float softplus_threshold, int flags) -> ()")
 
 
 def _verify_call(lib, capi, config, **over):
@@ -81,6 +86,34 @@ def test_capi_verify_rejects_before_launch(mutate, over, match):
 
     lib = capi.lib()
     rc = _verify_call(lib, capi, mutate(_good_config()), **over)
+    assert rc == capi.EINVAL
+    assert match in capi.last_error()
+
+
+@pytest.mark.parametrize(
+    "over,match",
+    [
+        (dict(A_log=None), "needs A_log"),
+        (dict(dt_bias=None), "gating needs A_log, dt_bias"),
+        (dict(sb=0.0), "softplus_beta > 0"),
+        (dict(sb=float("nan")), "softplus_beta > 0"),
+        (dict(gate=2), "the gate must be FP32"),  # fp16 raw a with bf16 activations
+        (dict(b=2), "beta must be FP32 or the activation dtype"),
+    ],
+)
+def test_capi_verify_gated_rejects_before_launch(over, match):
+    import ctypes
+
+    from gdn_recoverssm_b200 import capi
+
+    lib = capi.lib()
+    dummy = ctypes.c_void_p(256)  # never dereferenced: validation fails first
+    args = dict(A_log=dummy, dt_bias=dummy, sb=1.0, gate=capi.BF16, b=capi.F32)
+    args.update(over)
+    cfg = capi.int64_array(_good_config())
+    rc = lib.gdn_rssm_verify_gated(*([None] * 5), args["A_log"], args["dt_bias"], *([None] * 7), cfg, 28, 1.0,
+                                   args["sb"], 20.0, capi.BF16, capi.F32, args["gate"], args["b"], capi.F32, capi.I32,
+                                   capi.I32, 128, 128, capi.RECORD_PACKED, None)
     assert rc == capi.EINVAL
     assert match in capi.last_error()
 
@@ -150,6 +183,50 @@ def test_verify_argument_errors_raise_before_launch(change, match):
     g, beta, q, k, v = (kw.pop(n) for n in ("g", "beta", "q", "k", "v"))
     with pytest.raises(ValueError, match="GDN RecoverSSM: " + match):
         gdn_recoverssm_verify(g, beta, q, k, v, **kw)
+
+
+def _gated_inputs(**over):
+    kw = _verify_inputs()
+    g, beta = kw.pop("g"), kw.pop("beta")
+    kw.update(a=g, b=beta, A_log=torch.zeros(4), dt_bias=torch.zeros(4))
+    kw.update(over)
+    return kw
+
+
+@pytest.mark.parametrize(
+    "change,match",
+    [
+        (dict(A_log=torch.zeros(3)), "A_log or dt_bias shape is incompatible"),
+        (dict(dt_bias=torch.zeros(1, 4)), "A_log or dt_bias shape is incompatible"),
+        (dict(A_log=torch.zeros(4, dtype=torch.float64)), "A_log and dt_bias must be FP32"),
+        (dict(a=torch.zeros(1, 8, 4, dtype=torch.float16)), "a must be FP32 or the activation dtype"),
+        (dict(b=torch.zeros(1, 8, 3)), "gate or beta shape"),
+        (dict(softplus_beta=0.0), "softplus_beta must be positive"),
+        (dict(spec_query_len=0), r"spec_query_len must be in \[1, 8\]"),
+    ],
+)
+def test_verify_gated_argument_errors_raise_before_launch(change, match):
+    from gdn_recoverssm_b200 import gdn_recoverssm_verify_gated
+
+    kw = _gated_inputs(**change)
+    A_log, a, b, dt_bias, q, k, v = (kw.pop(n) for n in ("A_log", "a", "b", "dt_bias", "q", "k", "v"))
+    with pytest.raises(ValueError, match="GDN RecoverSSM: " + match):
+        gdn_recoverssm_verify_gated(A_log, a, b, dt_bias, q, k, v, **kw)
+
+
+def test_verify_gated_collects_one_native_launch():
+    from gdn_recoverssm_b200 import gdn_recoverssm_verify_gated
+
+    kw = _gated_inputs()
+    A_log, a, b, dt_bias, q, k, v = (kw.pop(n) for n in ("A_log", "a", "b", "dt_bias", "q", "k", "v"))
+    specs = []
+    gdn_recoverssm_verify_gated(A_log, a, b, dt_bias, q, k, v, softplus_beta=2.0, softplus_threshold=15.0,
+                                use_qk_l2norm_in_kernel=False, _collect=specs, **kw)
+    assert len(specs) == 1 and specs[0].name == "verify_gated"
+    args = specs[0].args
+    assert args[5] is not None and tuple(args[5].shape) == (4,)
+    assert args[14][:8] == [2, 8, 2, 4, 4, 5, 2, 0]
+    assert args[16:] == (2.0, 15.0, 1)  # softplus_beta, threshold, flags = packed records, no in-kernel norm
 
 
 def test_verify_collects_one_native_launch_without_running_it():
