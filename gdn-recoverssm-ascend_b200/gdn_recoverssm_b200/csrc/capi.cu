@@ -183,6 +183,9 @@ static int verify_impl(const void *q, const void *k, const void *v, const void *
               "value heads must be a positive multiple of the q/k heads");
   GDN_REQUIRE(p.query_len >= 1 && p.query_len <= kMaxWindow, "spec_query_len must be in [1, 8]");
   GDN_REQUIRE(p.tokens <= p.rows * p.query_len, "speculative decode input exceeds its activation capacity");
+  // the kernels keep row, token and page indices in 32 bits
+  GDN_REQUIRE(p.rows < (int64_t{1} << 31) - 1 && p.tokens < (int64_t{1} << 31) - 16 && p.blocks < (int64_t{1} << 31),
+              "rows, tokens and checkpoint blocks must stay below 2^31");
   GDN_REQUIRE(p.blocks > 0 && p.record_rows >= 1, "state pool and record rows must be non-empty");
   GDN_REQUIRE(p.rows * p.value_heads < (int64_t(1) << 31), "rows x value heads exceeds the launch grid");
   if (p.rows == 0 || p.tokens == 0) return GDN_RSSM_OK;

@@ -28,7 +28,8 @@
 //             bf16(X) -> the pass-2 operand, the Gram partial sums, the loads
 //             of the next units' slots and activations;
 //   thread 0: pass 2 right behind pass 1, one commit for both;
-//   all:      Gram coefficients; after the commit, thread 0 starts the NEXT
+//   warps 4+: Gram coefficients (warp 0, which issues the MMAs, does none of
+//             the per-unit scalar work); after the commit, thread 0 starts the NEXT
 //             unit's tile (4-D tensor map, 128-byte swizzle -- the layout
 //             the MMA's K-major descriptor reads directly -- one 128-row box
 //             per K slab) into the freed buffer, and every warp loads its 32
@@ -169,9 +170,9 @@ __device__ __forceinline__ void gram_finalize(const float (*part)[QT * QT], cons
 // (row, value head) of a CTA's units, advanced by gridDim.x units without a
 // 64-bit division per step.
 struct TcCursor {
-  int64_t row;
-  int64_t hv;
-  __device__ __forceinline__ void advance(int64_t dq, int64_t dr, int64_t HV) {
+  int32_t row;
+  int32_t hv;
+  __device__ __forceinline__ void advance(int32_t dq, int32_t dr, int32_t HV) {
     row += dq;
     hv += dr;
     if (hv >= HV) {
@@ -181,17 +182,25 @@ struct TcCursor {
   }
 };
 
+// A unit's row metadata, reduced to 32-bit fields when it is loaded (the host
+// keeps rows, tokens and blocks below 2^31): the token mask holds the window's
+// masking (t < Q, t < qlen, 0 <= bos + t < tokens), so bos only addresses valid
+// tokens and always fits; slot is -1 for a null or out-of-pool page.  Small
+// fields matter here: every register the walk keeps across units counts
+// against the 80 that three resident CTAs leave per thread.
 struct TcUnitMeta {
-  int64_t bos, qlen, slot;
+  int32_t bos, slot, vmask;
 };
 
-__device__ __forceinline__ int tc_valid_mask(const TcUnitMeta &m, int QT, int64_t Q, int64_t tokens) {
+__device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int64_t slot, int QT, int64_t Q,
+                                                   int64_t tokens, int64_t null_block, int64_t blocks) {
   int mask = 0;
   for (int t = 0; t < QT; ++t) {
-    const int64_t tok = m.bos + t;
-    if (t < Q && t < m.qlen && tok >= 0 && tok < tokens) mask |= 1 << t;
+    const int64_t tok = bos + t;
+    if (t < Q && t < eos - bos && tok >= 0 && tok < tokens) mask |= 1 << t;
   }
-  return mask;
+  const bool live = slot > null_block && slot < blocks;
+  return TcUnitMeta{mask ? static_cast<int32_t>(bos) : 0, live ? static_cast<int32_t>(slot) : -1, mask};
 }
 
 template <int QT, typename Act>
@@ -225,15 +234,13 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   Act *out = static_cast<Act *>(p.out);
 
   auto load_meta = [&](const TcCursor &c, bool in_range) {
-    TcUnitMeta m{0, 0, -1};
-    if (in_range) {
-      m.bos = load_typed_index(p.qsl, c.row * p.qsl_stride, p.qsl_dtype);
-      m.qlen = load_typed_index(p.qsl, (c.row + 1) * p.qsl_stride, p.qsl_dtype) - m.bos;
-      m.slot = load_typed_index(p.indices, c.row * p.index_stride, p.index_dtype);
-    }
-    return m;
+    if (!in_range) return TcUnitMeta{0, -1, 0};
+    const int64_t bos = load_typed_index(p.qsl, static_cast<int64_t>(c.row) * p.qsl_stride, p.qsl_dtype);
+    const int64_t eos = load_typed_index(p.qsl, static_cast<int64_t>(c.row + 1) * p.qsl_stride, p.qsl_dtype);
+    const int64_t slot = load_typed_index(p.indices, static_cast<int64_t>(c.row) * p.index_stride, p.index_dtype);
+    return tc_unit_meta(bos, eos, slot, QT, p.query_len, p.tokens, p.null_block, p.blocks);
   };
-  auto is_live = [&](const TcUnitMeta &m) { return m.slot > p.null_block && m.slot < p.blocks; };
+  auto is_live = [&](const TcUnitMeta &m) { return m.slot >= 0; };
   struct Inputs {  // one unit's activations in registers
     Act x[PER_WARP][EPL];  // q/k: vector warp + 8c, K elements 4 lane .. 4 lane + 3
     Act v[QT];             // v[t][r]
@@ -241,7 +248,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   };
   // Starts the loads of one unit's activations (nothing for null units).
   auto load_inputs = [&](Inputs &in, const TcCursor &c, const TcUnitMeta &m) {
-    const int vmask = is_live(m) ? tc_valid_mask(m, QT, p.query_len, p.tokens) : 0;
+    const int vmask = is_live(m) ? m.vmask : 0;
     const int hv = static_cast<int>(c.hv);
     const int h = hv / ratio;
 #pragma unroll
@@ -250,19 +257,22 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       const int t = j % QT;
       const bool live = j < NJ && ((vmask >> t) & 1);
       const Act *src = static_cast<const Act *>(j >= QT ? p.q : p.k);
-      const int64_t base = (m.bos + t) * (j >= QT ? p.q_ts : p.k_ts) + static_cast<int64_t>(h) * DIM + lane * EPL;
+      const int64_t base =
+          (static_cast<int64_t>(m.bos) + t) * (j >= QT ? p.q_ts : p.k_ts) + static_cast<int64_t>(h) * DIM + lane * EPL;
 #pragma unroll
       for (int e = 0; e < EPL; ++e) in.x[cc][e] = live ? src[base + e] : from_f32<Act>(0.f);
     }
     const Act *vin = static_cast<const Act *>(p.v);
 #pragma unroll
     for (int t = 0; t < QT; ++t)
-      in.v[t] = ((vmask >> t) & 1) ? vin[(m.bos + t) * p.v_ts + hv * DIM + r] : from_f32<Act>(0.f);
+      in.v[t] = ((vmask >> t) & 1) ? vin[(static_cast<int64_t>(m.bos) + t) * p.v_ts + hv * DIM + r]
+                                   : from_f32<Act>(0.f);
     in.g = 0.f;
     in.beta = 0.f;
     if (tid < QT && ((vmask >> tid) & 1)) {
-      in.g = load_float(p.g, (m.bos + tid) * p.g_ts + hv, p.gate_dtype);
-      in.beta = load_float(p.beta, (m.bos + tid) * p.beta_ts + hv, p.beta_dtype);
+      const int64_t tok = static_cast<int64_t>(m.bos) + tid;
+      in.g = load_float(p.g, tok * p.g_ts + hv, p.gate_dtype);
+      in.beta = load_float(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
     }
   };
   auto issue_tile = [&](const TcCursor &c, const TcUnitMeta &m) {  // thread 0
@@ -274,12 +284,13 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   };
 
   // ---- walk: cursors and metadata of units i, i + 1, i + 2 ------------------ //
-  const int64_t dq = G / HV, dr = G % HV;
-  TcCursor c0{static_cast<int64_t>(blockIdx.x) / HV, static_cast<int64_t>(blockIdx.x) % HV};
+  const int32_t HV32 = static_cast<int32_t>(HV);
+  const int32_t dq = static_cast<int32_t>(G / HV), dr = static_cast<int32_t>(G % HV);
+  TcCursor c0{static_cast<int32_t>(blockIdx.x / HV32), static_cast<int32_t>(blockIdx.x % HV32)};
   TcCursor c1 = c0;
-  c1.advance(dq, dr, HV);
+  c1.advance(dq, dr, HV32);
   TcCursor c2 = c1;
-  c2.advance(dq, dr, HV);
+  c2.advance(dq, dr, HV32);
   TcUnitMeta m0 = load_meta(c0, true), m1 = load_meta(c1, blockIdx.x + G < units);
 
   if (tid == 0) {
@@ -315,7 +326,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     const int64_t row = c0.row;
     const int hv = static_cast<int>(c0.hv);
     const int h = hv / ratio;
-    const int vmask = tc_valid_mask(m0, QT, p.query_len, p.tokens);
+    const int vmask = m0.vmask;
     const bool rec_ok = row < p.record_rows;
     Window &w = sm.win[i & 1];
 
@@ -324,7 +335,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       prefetch();
       for (int e = tid; e < QT * DIM; e += kVerifyThreads) {
         const int t = e / DIM;
-        if ((vmask >> t) & 1) out[(m0.bos + t) * p.out_ts + hv * DIM + (e % DIM)] = from_f32<Act>(0.f);
+        if ((vmask >> t) & 1)
+          out[(static_cast<int64_t>(m0.bos) + t) * p.out_ts + hv * DIM + (e % DIM)] = from_f32<Act>(0.f);
       }
       // the next unit's tile (this unit started none)
       if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
@@ -416,21 +428,21 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       {
         const int kh = warp >> 2;
         const unsigned char *row_base = tile + r * 128;
-        uint32_t packed_lo[32];
 #pragma unroll
-        for (int mm = 0; mm < 2; ++mm) {
+        for (int mm = 0; mm < 2; ++mm) {  // one 32-element K slab (16 packed columns) at a time
           const int m = 2 * kh + mm;
+          uint32_t packed_lo[16];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float4 x = *reinterpret_cast<const float4 *>(row_base + m * Sh::SLAB + ((c ^ (r & 7)) << 4));
             const __nv_bfloat162 lo01 = __floats2bfloat162_rn(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y));
             const __nv_bfloat162 lo23 = __floats2bfloat162_rn(x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
-            packed_lo[mm * 16 + 2 * c] = *reinterpret_cast<const uint32_t *>(&lo01);
-            packed_lo[mm * 16 + 2 * c + 1] = *reinterpret_cast<const uint32_t *>(&lo23);
+            packed_lo[2 * c] = *reinterpret_cast<const uint32_t *>(&lo01);
+            packed_lo[2 * c + 1] = *reinterpret_cast<const uint32_t *>(&lo23);
           }
+          __syncwarp();  // tcgen05.st is warp-wide (.sync.aligned)
+          ptx::tmem_st16_u(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::A_LO + 32u * kh + 16u * mm, packed_lo);
         }
-        __syncwarp();  // tcgen05.st is warp-wide (.sync.aligned)
-        ptx::tmem_st32_u(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::A_LO + 32u * kh, packed_lo);
         ptx::tmem_wait_st();
       }
       // ---- ... the pass-2 operand bf16(X): G2 8-row groups per 64-element slab ---- //
@@ -473,9 +485,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         }
         ptx::mma_commit(&sm.mma_bar);
       }
-      // ---- Gram coefficients and decay products of this window ---------------- //
-      if (tid < QT * QT) gram_finalize<QT>(sm.gpart, w.dec, w.mkk, w.mkq, tid);
-      if (tid == 32) {
+      // ---- Gram coefficients and decay products (off warp 0, which issues) ---- //
+      if (tid >= 128 && tid < 128 + QT * QT) gram_finalize<QT>(sm.gpart, w.dec, w.mkk, w.mkq, tid - 128);
+      if (tid == 224) {
         float a = 1.f;
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
@@ -516,7 +528,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           float o = w.A[t] * ((d[QT + t] + d[NJ + QT + t]) + d2[QT + t]);
 #pragma unroll
           for (int s2 = 0; s2 <= t; ++s2) o = fmaf(w.mkq[t][s2], cr[s2], o);
-          out[(m0.bos + t) * p.out_ts + hv * DIM + r] = from_f32<Act>(o);
+          out[(static_cast<int64_t>(m0.bos) + t) * p.out_ts + hv * DIM + r] = from_f32<Act>(o);
         }
       }
     }
@@ -525,7 +537,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     m1 = m2;
     c0 = c1;
     c1 = c2;
-    c2.advance(dq, dr, HV);
+    c2.advance(dq, dr, HV32);
   }
   // ---- release tensor memory (every path after the allocation) ---------------- //
   ptx::tc_fence_before_sync();
