@@ -259,7 +259,7 @@ def run_b200(args):
         t_end.record(stream)
         barrier()
         # end to end through the public API with host buffers
-        e2e = _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier)
+        e2e = _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=args.e2e_buffers)
     total_ms = t_start.elapsed_time(t_end)
     verify_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
     plan_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
@@ -311,23 +311,40 @@ def run_b200(args):
     return 0
 
 
-def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier):
-    """Same step through the public API from pinned host buffers, as a
-    serving loop runs it: every step copies its inputs (q, k, v, g, beta and
-    the row metadata) host -> device, runs verify + commit, and copies the
-    attention output device -> host.  Copies go on their own streams into
-    double-buffered device tensors, so the H2D of step i + 1 and the D2H of
-    step i - 1 overlap the compute of step i; all of it is inside the timed
-    region (from the first H2D to the last D2H)."""
+def _arena_views(buf, layout):
+    """Typed views of one flat uint8 buffer, ``layout`` = [(name, offset, dtype, shape)]."""
+    views = {}
+    for name, off, dtype, shape in layout:
+        n = int(torch.Size(shape).numel()) * torch.empty((), dtype=dtype).element_size()
+        views[name] = buf.narrow(0, off, n).view(dtype).view(shape)
+    return views
+
+
+def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=3):
+    """Same step through the public API from pinned host memory, as a serving
+    loop runs it: every step copies its inputs (q, k, v, g, beta and the row
+    metadata, packed in one pinned staging buffer) host -> device in one copy,
+    runs verify + commit, and copies the attention output device -> host.
+    Copies go on their own streams into ``nbuf`` device buffers, so the H2D of
+    step i + 1 and the D2H of step i - 1 overlap the compute of step i; all of
+    it is inside the timed region (from the first H2D to the last D2H)."""
     names = ["q", "k", "v", "g", "beta", "qsl", "state_indices", "accepted"]
     if align_kw:
         names += ["block_table", "num_computed"]
-    host = {n: getattr(wl, n).cpu().pin_memory() for n in names}
-    nbuf = 2
-    dev_in = [{n: torch.empty_like(t, device=dev) for n, t in host.items()} for _ in range(nbuf)]
+    layout, off = [], 0
+    for n in names:
+        t = getattr(wl, n)
+        layout.append((n, off, t.dtype, tuple(t.shape)))
+        off += (t.numel() * t.element_size() + 255) // 256 * 256
+    h2d = off
+    host_buf = torch.empty(h2d, dtype=torch.uint8).pin_memory()
+    host = _arena_views(host_buf, layout)
+    for n in names:
+        host[n].copy_(getattr(wl, n).cpu())
+    dev_buf = [torch.empty(h2d, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
+    dev_in = [_arena_views(b, layout) for b in dev_buf]
     out_dev = [torch.empty_like(wl.out) for _ in range(nbuf)]
     out_host = [torch.empty(wl.out.shape, dtype=wl.out.dtype).pin_memory() for _ in range(nbuf)]
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = out_host[0].numel() * out_host[0].element_size()
     steps = max(4, args.steps // 4)
     h2d_stream = torch.cuda.Stream(dev)
@@ -341,8 +358,7 @@ def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier):
         d = dev_in[b]
         h2d_stream.wait_event(ev_done[b])  # the step that last read buffer b is done
         with torch.cuda.stream(h2d_stream):
-            for n, t in host.items():
-                d[n].copy_(t, non_blocking=True)
+            dev_buf[b].copy_(host_buf, non_blocking=True)
             ev_in[b].record(h2d_stream)
         stream.wait_event(ev_in[b])
         stream.wait_event(ev_out[b])  # out_dev[b] has been copied out
@@ -360,7 +376,7 @@ def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier):
             out_host[b].copy_(out_dev[b], non_blocking=True)
             ev_out[b].record(d2h_stream)
 
-    for i in range(3):
+    for i in range(nbuf + 1):
         step(i)
     torch.cuda.synchronize(dev)
     barrier()
@@ -389,6 +405,7 @@ def main(argv=None):
     ap.add_argument("--reference-budget-s", type=float, default=60.0,
                     help="CPU seconds the --impl reference run may spend over all its steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-buffers", type=int, default=3, help="device input/output buffers of the end-to-end loop")
     ap.add_argument("--rows", type=int, default=None, help="reduced batch (profiling cases only)")
     ap.add_argument("--pool", type=int, default=None, help="reduced state pool (profiling cases only)")
     args = ap.parse_args(argv)
