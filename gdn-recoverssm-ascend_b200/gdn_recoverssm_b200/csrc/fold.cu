@@ -25,10 +25,21 @@ int launch_fold_variant(FoldParams p, cudaStream_t stream) {
     GDN_CUDA(cudaFuncSetAttribute(fold_kernel<DIM, St, Kt>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev] = true;
   }
-  // one CTA per (layer, row, value head) unit
+  // one CTA per (layer, row, value head) unit, launched as a programmatic
+  // dependent of the kernel before it (the plan): its CTAs become resident
+  // while the plan runs and wait in the kernel for the plan's results
   const int64_t grid = p.layers * p.rows * p.heads;
-  fold_kernel<DIM, St, Kt><<<static_cast<unsigned>(grid), kFoldThreads, smem, stream>>>(p);
-  GDN_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kFoldThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  GDN_CUDA(cudaLaunchKernelEx(&cfg, fold_kernel<DIM, St, Kt>, p));
   return GDN_RSSM_OK;
 }
 

@@ -16,11 +16,13 @@
 #pragma once
 
 #include "params.cuh"
+#include "ptx.cuh"
 
 namespace gdn_rssm {
 
 
 __global__ void commit_plan_kernel(const CommitPlanParams p) {
+  ptx::launch_dependents();  // the fold may start launching (it waits for this grid)
   const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (r >= p.rows) return;
   const int64_t nul = p.null_block;
@@ -66,6 +68,7 @@ __global__ void commit_plan_kernel(const CommitPlanParams p) {
 
 
 __global__ void grouped_plan_kernel(const GroupedPlanParams p) {
+  ptx::launch_dependents();  // the fold may start launching (it waits for this grid)
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (row >= p.rows) return;
   const int64_t nul = p.null_block;

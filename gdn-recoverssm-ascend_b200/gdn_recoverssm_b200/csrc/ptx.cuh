@@ -17,6 +17,13 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch: a primary kernel lets the next kernel in the
+// stream start launching; that kernel waits for the primary's completion (and
+// its memory) before reading what it wrote.  Both are no-ops without such a
+// launch pairing.
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void wait_prerequisite_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Makes the barrier initialisation visible to the async (TMA) proxy.
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
