@@ -74,16 +74,32 @@ int launch_fold(const FoldParams &p, int dim, int32_t state_dtype, int32_t key_d
 
 static unsigned blocks_for(int64_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
 
-int launch_commit_plan(const CommitPlanParams &p, cudaStream_t stream) {
-  commit_plan_kernel<<<blocks_for(p.rows, 128), 128, 0, stream>>>(p);
-  GDN_CUDA(cudaGetLastError());
+// Launch as a programmatic dependent of the previous kernel in the stream: the
+// kernel waits in its prologue (griddepcontrol.wait) for that grid's
+// completion and memory, so only the launch latency overlaps.
+template <typename Params>
+static int launch_dependent(void (*kernel)(Params), const Params &p, unsigned grid, unsigned threads,
+                            cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  GDN_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
   return GDN_RSSM_OK;
 }
 
+int launch_commit_plan(const CommitPlanParams &p, cudaStream_t stream) {
+  return launch_dependent(commit_plan_kernel, p, blocks_for(p.rows, 128), 128, stream);
+}
+
 int launch_grouped_plan(const GroupedPlanParams &p, cudaStream_t stream) {
-  grouped_plan_kernel<<<blocks_for(p.rows, 128), 128, 0, stream>>>(p);
-  GDN_CUDA(cudaGetLastError());
-  return GDN_RSSM_OK;
+  return launch_dependent(grouped_plan_kernel, p, blocks_for(p.rows, 128), 128, stream);
 }
 
 int launch_publish_align(const PublishParams &p, cudaStream_t stream) {

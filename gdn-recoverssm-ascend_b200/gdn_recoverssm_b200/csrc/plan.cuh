@@ -22,7 +22,11 @@ namespace gdn_rssm {
 
 
 __global__ void commit_plan_kernel(const CommitPlanParams p) {
-  ptx::launch_dependents();  // the fold may start launching (it waits for this grid)
+  // launched as a programmatic dependent of the kernel before it (the sampler
+  // in serving, verify in a bench step): wait for it before reading its
+  // results, then let the fold start launching (it waits for this grid)
+  ptx::wait_prerequisite_grid();
+  ptx::launch_dependents();
   const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (r >= p.rows) return;
   const int64_t nul = p.null_block;
@@ -68,7 +72,8 @@ __global__ void commit_plan_kernel(const CommitPlanParams p) {
 
 
 __global__ void grouped_plan_kernel(const GroupedPlanParams p) {
-  ptx::launch_dependents();  // the fold may start launching (it waits for this grid)
+  ptx::wait_prerequisite_grid();  // as in commit_plan_kernel
+  ptx::launch_dependents();
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (row >= p.rows) return;
   const int64_t nul = p.null_block;

@@ -197,6 +197,7 @@ constexpr int verify_min_blocks() {
 template <int DIM, int QT, typename Act, typename St>
 __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
     verify_kernel(const __grid_constant__ CUtensorMap state_map, const VerifyParams p) {
+  ptx::launch_dependents();  // a commit plan behind it may launch; it waits for this grid
   using Sh = VerifyShape<DIM, QT, Act, St>;
   using Small = typename Sh::Small;
   constexpr int NJ = Sh::NJ, EPC = Sh::EPC, BOXW = Sh::BOXW, R = Sh::R, EPL = Sh::EPL, V = Sh::V;

@@ -206,6 +206,7 @@ __device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int
 template <int QT, typename Act>
 __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     verify_tc_kernel(const __grid_constant__ CUtensorMap state_map, const VerifyParams p) {
+  ptx::launch_dependents();  // a commit plan behind it may launch; it waits for this grid
   using Sh = VerifyTcShape<QT, Act>;
   using Small = typename Sh::Small;
   using Window = typename Sh::Window;
