@@ -112,9 +112,11 @@ def _dist():
     return world, rank, local
 
 
-def cpu_baseline(cfg, *, rows_sample, seed=0, repeats=1):
+def cpu_baseline(cfg, *, rows_sample, seed=0, repeats=1, gated=False):
     """Time the oracle's torch CPU executors (all host threads) on a bounded
-    sample of the workload: `rows_sample` sequence rows with every head."""
+    sample of the workload: `rows_sample` sequence rows with every head
+    (with ``gated``, the gates are computed from raw a, b inside the timed
+    region, as the fused-gating verify does)."""
     from gdn_recoverssm_b200 import synthetic
     from oracle import cpu_executors as X
 
@@ -129,6 +131,10 @@ def cpu_baseline(cfg, *, rows_sample, seed=0, repeats=1):
     v = torch.randn(T, HV, D, generator=gen).to(act)
     g = -torch.nn.functional.softplus(torch.randn(T, HV, generator=gen))
     beta = torch.sigmoid(torch.randn(T, HV, generator=gen))
+    a_raw = torch.randn(T, HV, generator=gen).to(act)
+    b_raw = torch.randn(T, HV, generator=gen).to(act)
+    A_log = torch.log(torch.rand(HV, generator=gen) * 15.0 + 1.0)
+    dt_bias = torch.full((HV,), -4.0)
     pool = 2 * B + 1
     state = torch.randn(pool, HV, D, D, generator=gen) * 0.1
     src = torch.arange(1, B + 1, dtype=torch.int32)
@@ -141,6 +147,9 @@ def cpu_baseline(cfg, *, rows_sample, seed=0, repeats=1):
     times = []
     for _ in range(repeats):
         t0 = time.perf_counter()
+        if gated:
+            g = -torch.exp(A_log) * torch.nn.functional.softplus(a_raw.float() + dt_bias)
+            beta = torch.sigmoid(b_raw.float())
         X.verify_packed(q, k, v, g, beta, state, qsl, src, records, out, spec_query_len=Q, scale=D**-0.5)
         X.fold_packed(state, records, src, acc, fin, zeros, zeros, rows=B)
         times.append(time.perf_counter() - t0)
@@ -158,21 +167,21 @@ def run_reference(args):
 
     spec = synthetic.CONFIGS[args.config]
     # size each step's sample so that warm-up + K steps fit the time budget
-    probe = cpu_baseline(args.config, rows_sample=4)
+    probe = cpu_baseline(args.config, rows_sample=4, gated=args.gated)
     per_row = probe["seconds_per_sample"] / 4
     budget = args.reference_budget_s / max(1, args.steps + min(args.warmup, 1))
     rows = int(max(1, min(spec["B"], budget / per_row)))
     if args.warmup > 0:
-        cpu_baseline(args.config, rows_sample=rows)
+        cpu_baseline(args.config, rows_sample=rows, gated=args.gated)
     vals = []
     for _ in range(args.steps):
-        vals.append(cpu_baseline(args.config, rows_sample=rows)["value"])
+        vals.append(cpu_baseline(args.config, rows_sample=rows, gated=args.gated)["value"])
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * spec["B"] / value, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": _config_dict(args.config, world),
+        "config": _config_dict(args.config, world, args.gated),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                          "sample": f"each step: {rows} of {spec['B']} rows x all heads (verify + fold), torch CPU "
                                    f"executors restating the reference's CPU path"},
@@ -182,7 +191,7 @@ def run_reference(args):
     return 0
 
 
-def _config_dict(cfg, world):
+def _config_dict(cfg, world, gated=False):
     from gdn_recoverssm_b200 import synthetic
 
     s = synthetic.CONFIGS[cfg]
@@ -194,6 +203,8 @@ def _config_dict(cfg, world):
         "spec_query_len": s["Q"],
         "parallelism": f"v-head shards x{world} (no collective)",
         "l2": "inputs larger than L2: every step reads all B x HV state tiles (64 KiB each)",
+        "gates": ("fused in the verify prologue from raw a, b (activation dtype) and per-head A_log, dt_bias"
+                  if gated else "precomputed: g (fp32 log-space decay), beta (fp32)"),
     }
 
 
@@ -210,7 +221,8 @@ def run_b200(args):
     from gdn_recoverssm_b200 import _native, synthetic
 
     _native.ops()
-    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=16, rows=args.rows, pool=args.pool)
+    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=16, rows=args.rows, pool=args.pool,
+                        gated=args.gated)
     stream = torch.cuda.current_stream(dev)
     ctx = g.GDNRecoverSSMCommitContext.from_tensors([wl.conv], [wl.state], [wl.records], spec_query_len=wl.Q,
                                                     max_num_reqs=wl.B)
@@ -220,9 +232,15 @@ def run_b200(args):
                         mamba_block_size=wl.block_size)
 
     def verify():
-        g.gdn_recoverssm_verify(wl.g, wl.beta, wl.q, wl.k, wl.v, checkpoint_state=wl.state, replay_cache=wl.records,
-                                query_start_loc=wl.qsl, state_indices=wl.state_indices, spec_query_len=wl.Q,
-                                out=wl.out)
+        if args.gated:
+            g.gdn_recoverssm_verify_gated(wl.A_log, wl.a, wl.b, wl.dt_bias, wl.q, wl.k, wl.v,
+                                          checkpoint_state=wl.state, replay_cache=wl.records, query_start_loc=wl.qsl,
+                                          state_indices=wl.state_indices, spec_query_len=wl.Q,
+                                          use_qk_l2norm_in_kernel=False, out=wl.out)
+        else:
+            g.gdn_recoverssm_verify(wl.g, wl.beta, wl.q, wl.k, wl.v, checkpoint_state=wl.state,
+                                    replay_cache=wl.records, query_start_loc=wl.qsl, state_indices=wl.state_indices,
+                                    spec_query_len=wl.Q, out=wl.out)
 
     specs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=False, **align_kw)
     plan_spec, fold_spec = specs[0], specs[-1]
@@ -297,7 +315,7 @@ def run_b200(args):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": _config_dict(args.config, world),
+        "data": "synthetic", "config": _config_dict(args.config, world, args.gated),
         "e2e": {"value": wl.B / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms},
         "roofline": {"bound": "hbm", "kernel": "fold (grouped commit)", "achieved": fold_gbs, "peak": peak,
@@ -314,7 +332,7 @@ def run_b200(args):
         "device_status": status,
     }
     if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline(args.config, rows_sample=args.cpu_rows)
+        line["cpu_baseline"] = cpu_baseline(args.config, rows_sample=args.cpu_rows, gated=args.gated)
     print(json.dumps(line))
     return 0
 
@@ -336,7 +354,8 @@ def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=3):
     Copies go on their own streams into ``nbuf`` device buffers, so the H2D of
     step i + 1 and the D2H of step i - 1 overlap the compute of step i; all of
     it is inside the timed region (from the first H2D to the last D2H)."""
-    names = ["q", "k", "v", "g", "beta", "qsl", "state_indices", "accepted"]
+    gated = wl.a is not None
+    names = ["q", "k", "v"] + (["a", "b"] if gated else ["g", "beta"]) + ["qsl", "state_indices", "accepted"]
     if align_kw:
         names += ["block_table", "num_computed"]
     layout, off = [], 0
@@ -374,9 +393,13 @@ def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=3):
         if align_kw:
             kw = dict(block_table=d["block_table"], num_computed_tokens=d["num_computed"],
                       mamba_block_size=wl.block_size)
-        g.gdn_recoverssm_verify(d["g"], d["beta"], d["q"], d["k"], d["v"], checkpoint_state=wl.state,
-                                replay_cache=wl.records, query_start_loc=d["qsl"], state_indices=d["state_indices"],
-                                spec_query_len=wl.Q, out=out_dev[b])
+        common = dict(checkpoint_state=wl.state, replay_cache=wl.records, query_start_loc=d["qsl"],
+                      state_indices=d["state_indices"], spec_query_len=wl.Q, out=out_dev[b])
+        if gated:  # A_log / dt_bias are layer weights: resident, not copied per step
+            g.gdn_recoverssm_verify_gated(wl.A_log, d["a"], d["b"], wl.dt_bias, d["q"], d["k"], d["v"],
+                                          use_qk_l2norm_in_kernel=False, **common)
+        else:
+            g.gdn_recoverssm_verify(d["g"], d["beta"], d["q"], d["k"], d["v"], **common)
         ctx.commit(d["accepted"], d["state_indices"], d["qsl"], commit_conv=False, **kw)
         ev_done[b].record(stream)
         d2h_stream.wait_event(ev_done[b])
@@ -413,6 +436,8 @@ def main(argv=None):
     ap.add_argument("--reference-budget-s", type=float, default=60.0,
                     help="CPU seconds the --impl reference run may spend over all its steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gated", action="store_true",
+                    help="verify through the fused-gating entry point (raw a, b, A_log, dt_bias)")
     ap.add_argument("--e2e-buffers", type=int, default=3, help="device input/output buffers of the end-to-end loop")
     ap.add_argument("--rows", type=int, default=None, help="reduced batch (profiling cases only)")
     ap.add_argument("--pool", type=int, default=None, help="reduced state pool (profiling cases only)")

@@ -72,15 +72,21 @@ constexpr uint32_t kGateInKernel = 1u << 8;
 // Decay exp(g) and beta of value head hv from the two values loaded from the
 // g and beta slots.  Gated: g = -exp(A_log) * softplus(a + dt_bias) with
 // softplus(x) = log1p(exp(sb x)) / sb below the threshold and x above it,
-// beta = sigmoid(b).
-__device__ __forceinline__ void token_gates(const VerifyParams &p, int hv, float graw, float braw, float &dec,
-                                            float &bet) {
+// beta = sigmoid(b).  a_log / dt_bias are the head's A_log and dt_bias
+// (read only when gated).
+__device__ __forceinline__ void gate_math(const VerifyParams &p, float a_log, float dt_bias, float a, float b,
+                                          float &dec, float &bet) {
+  const float x = a + dt_bias;
+  const float bx = p.softplus_beta * x;
+  const float sp = bx <= p.softplus_threshold ? log1pf(expf(bx)) / p.softplus_beta : x;
+  dec = expf(-expf(a_log) * sp);
+  bet = 1.f / (1.f + expf(-b));
+}
+
+__device__ __forceinline__ void token_gates(const VerifyParams &p, float a_log, float dt_bias, float graw,
+                                            float braw, float &dec, float &bet) {
   if (p.flags & kGateInKernel) {
-    const float x = graw + p.dt_bias[hv];
-    const float bx = p.softplus_beta * x;
-    const float sp = bx <= p.softplus_threshold ? log1pf(expf(bx)) / p.softplus_beta : x;
-    dec = expf(-expf(p.A_log[hv]) * sp);
-    bet = 1.f / (1.f + expf(-braw));
+    gate_math(p, a_log, dt_bias, graw, braw, dec, bet);
   } else {
     dec = expf(graw);
     bet = braw;
@@ -286,9 +292,12 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_min_blocks<QT>())
       vv[c] = (i < QT * DIM && ((valid_mask >> t) & 1)) ? vin[(bos + t) * p.v_ts + hv * DIM + e] : from_f32<Act>(0.f);
     }
     float dec = 1.f, bet = 0.f;
-    if (tid < QT && ((valid_mask >> tid) & 1))
-      token_gates(p, hv, load_float(p.g, (bos + tid) * p.g_ts + hv, p.gate_dtype),
+    if (tid < QT && ((valid_mask >> tid) & 1)) {
+      const bool gated = (p.flags & kGateInKernel) != 0;
+      token_gates(p, gated ? p.A_log[hv] : 0.f, gated ? p.dt_bias[hv] : 0.f,
+                  load_float(p.g, (bos + tid) * p.g_ts + hv, p.gate_dtype),
                   load_float(p.beta, (bos + tid) * p.beta_ts + hv, p.beta_dtype), dec, bet);
+    }
 #pragma unroll
     for (int c = 0; c < VPER; ++c) {
       const int i = tid + c * kVerifyThreads;

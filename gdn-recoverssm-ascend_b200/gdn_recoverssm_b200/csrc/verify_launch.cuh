@@ -48,23 +48,25 @@ int launch_verify_variant(VerifyLaunch &L) {
                             L.state_bs, L.state_hs, L.state_vs);
   if (rc != GDN_RSSM_OK) return rc;
   constexpr int smem = tc ? verify_tc_smem_bytes<QT, Act>() : verify_smem_bytes<DIM, QT, Act, St>();
-  auto kernel = [] {
-    if constexpr (tc) {
-      return verify_tc_kernel<QT, Act>;
-    } else {
-      return verify_kernel<DIM, QT, Act, St>;
-    }
-  }();
-  static bool configured[64] = {false};
+  // the tensor-core kernel has a separate instantiation for the fused gating
+  // prologue, so the plain form keeps its register budget
+  const int gated = (L.p.flags & kGateInKernel) ? 1 : 0;
+  void (*kernel)(const CUtensorMap, const VerifyParams) = nullptr;
+  if constexpr (tc) {
+    kernel = gated ? verify_tc_kernel<QT, Act, true> : verify_tc_kernel<QT, Act, false>;
+  } else {
+    kernel = verify_kernel<DIM, QT, Act, St>;
+  }
+  static bool configured[2][64] = {};
   int dev = 0;
   GDN_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) {
     set_error("GDN RecoverSSM: device ordinal out of range");
     return GDN_RSSM_EUNSUPPORTED;
   }
-  if (!configured[dev]) {
+  if (!configured[gated][dev]) {
     GDN_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured[dev] = true;
+    configured[gated][dev] = true;
   }
   const int64_t units = L.p.rows * L.p.value_heads;
   if (units <= 0) return GDN_RSSM_OK;

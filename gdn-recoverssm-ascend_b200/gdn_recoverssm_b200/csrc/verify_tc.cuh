@@ -203,7 +203,8 @@ __device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int
   return TcUnitMeta{mask ? static_cast<int32_t>(bos) : 0, live ? static_cast<int32_t>(slot) : -1, mask};
 }
 
-template <int QT, typename Act>
+// GATED: the fused gating prologue (raw a, b in the g / beta slots).
+template <int QT, typename Act, bool GATED>
 __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     verify_tc_kernel(const __grid_constant__ CUtensorMap state_map, const VerifyParams p) {
   ptx::launch_dependents();  // a commit plan behind it may launch; it waits for this grid
@@ -245,8 +246,13 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   struct Inputs {  // one unit's activations in registers
     Act x[PER_WARP][EPL];  // q/k: vector warp + 8c, K elements 4 lane .. 4 lane + 3
     Act v[QT];             // v[t][r]
-    float g, beta;         // token tid (tid < QT)
+    // g / beta of token t on thread GT + t (t < QT); gated: raw a / b there,
+    // and the head's A_log / dt_bias on thread GT + QT
+    float g, beta;
   };
+  // plain: warp 0 turns g into the decay while staging; gated: warp 1 runs
+  // the gating prologue in the pass-1 window, where it has slack
+  constexpr int GT = GATED ? 32 : 0;
   // Starts the loads of one unit's activations (nothing for null units).
   auto load_inputs = [&](Inputs &in, const TcCursor &c, const TcUnitMeta &m) {
     const int vmask = is_live(m) ? m.vmask : 0;
@@ -270,10 +276,14 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
                                    : from_f32<Act>(0.f);
     in.g = 0.f;
     in.beta = 0.f;
-    if (tid < QT && ((vmask >> tid) & 1)) {
-      const int64_t tok = static_cast<int64_t>(m.bos) + tid;
+    const int gt = tid - GT;
+    if (gt >= 0 && gt < QT && ((vmask >> gt) & 1)) {
+      const int64_t tok = static_cast<int64_t>(m.bos) + gt;
       in.g = load_float(p.g, tok * p.g_ts + hv, p.gate_dtype);
       in.beta = load_float(p.beta, tok * p.beta_ts + hv, p.beta_dtype);
+    } else if (GATED && gt == QT && vmask != 0) {
+      in.g = p.A_log[hv];  // handed to the token lanes by a shuffle
+      in.beta = p.dt_bias[hv];
     }
   };
   auto issue_tile = [&](const TcCursor &c, const TcUnitMeta &m) {  // thread 0
@@ -344,13 +354,26 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       __syncthreads();  // the previous unit's recurrence is done with its window buffer
     } else {
       // ---- stage the window --------------------------------------------------- //
-      if (tid < QT) {
-        const bool live = (vmask >> tid) & 1;
+      // decay and beta of the window -> shared memory (read after the next CTA
+      // barrier) and the decay records
+      auto stage_gates = [&](float a_log, float dt_bias) {
+        const int t = tid - GT;
+        const bool live = (vmask >> t) & 1;
         float dec = 1.f, bet = 0.f;
-        if (live) token_gates(p, hv, ic.g, ic.beta, dec, bet);
-        w.dec[tid] = dec;
-        w.beta[tid] = bet;
-        if (rec_ok && live) p.decay[row * p.decay_rs + hv * p.decay_hs + tid * p.decay_ts] = dec;
+        if (live) {
+          if constexpr (GATED) {
+            gate_math(p, a_log, dt_bias, ic.g, ic.beta, dec, bet);
+          } else {
+            dec = expf(ic.g);
+            bet = ic.beta;
+          }
+        }
+        w.dec[t] = dec;
+        w.beta[t] = bet;
+        if (rec_ok && live) p.decay[row * p.decay_rs + hv * p.decay_hs + t * p.decay_ts] = dec;
+      };
+      if constexpr (!GATED) {
+        if (tid < QT) stage_gates(0.f, 0.f);
       }
       if constexpr (NB > 2 * NJ) {  // zero padding rows of B (Q < 4)
         constexpr int PAD = (NB - 2 * NJ) * 8;  // 16-byte chunks per slab
@@ -445,6 +468,13 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           ptx::tmem_st16_u(tmem + (static_cast<uint32_t>(qd * 32) << 16) + Sh::A_LO + 32u * kh + 16u * mm, packed_lo);
         }
         ptx::tmem_wait_st();
+      }
+      if constexpr (GATED) {
+        if (warp == 1) {
+          const float a_log = __shfl_sync(0xffffffffu, ic.g, QT);  // the head's constants, from lane QT
+          const float dt_bias = __shfl_sync(0xffffffffu, ic.beta, QT);
+          if (lane < QT) stage_gates(a_log, dt_bias);
+        }
       }
       // ---- ... the pass-2 operand bf16(X): G2 8-row groups per 64-element slab ---- //
 #pragma unroll

@@ -67,6 +67,12 @@ class Workload:
     num_computed: torch.Tensor | None = None
     block_size: int | None = None
     conv: torch.Tensor | None = None
+    # raw gate inputs of the fused-gating verify (make(..., gated=True)):
+    # a, b [T, HV] in the activation dtype; A_log, dt_bias [HV] fp32
+    a: torch.Tensor | None = None
+    b: torch.Tensor | None = None
+    A_log: torch.Tensor | None = None
+    dt_bias: torch.Tensor | None = None
     extra: dict = field(default_factory=dict)
 
     @property
@@ -151,9 +157,12 @@ def metadata(cfg: int, seed: int = 0, rows: int | None = None, pool: int | None 
 
 
 def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv_dim: int = 0,
-         rows: int | None = None, pool: int | None = None) -> Workload:
+         rows: int | None = None, pool: int | None = None, gated: bool = False) -> Workload:
     """Allocate and fill one configuration's tensors on ``device`` (this
-    rank's head shard)."""
+    rank's head shard).  ``gated`` adds the raw gate inputs of the
+    fused-gating verify: a, b ~ N(0, 1) in the activation dtype, A_log =
+    log(U(1, 16)) and dt_bias = softplus^-1(dt) with dt log-uniform in
+    [1e-3, 1e-1] per value head."""
     spec = spec_of(cfg, rows, pool)
     B, H, HV, D, Q, pool = spec["B"], spec["H"], spec["HV"], spec["D"], spec["Q"], spec["pool"]
     shard = head_shard(H, HV, world, rank)
@@ -187,17 +196,25 @@ def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv
         wl.block_size = meta["block_size"]
     if conv_dim:
         wl.conv = torch.randn(pool, conv_dim, 3 + Q - 1, generator=gen, device=dev).to(act)
+    if gated:
+        wl.a = torch.randn(T, HV, generator=gen, device=dev).to(act)
+        wl.b = torch.randn(T, HV, generator=gen, device=dev).to(act)
+        wl.A_log = torch.log(torch.rand(HV, generator=gen, device=dev) * 15.0 + 1.0)
+        dt = torch.exp(torch.rand(HV, generator=gen, device=dev) * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
+        wl.dt_bias = dt + torch.log(-torch.expm1(-dt))
     wl.extra["meta"] = meta
     return wl
 
 
 def verify_bytes(wl: Workload, units: int | None = None) -> int:
     """Algorithmic bytes of one verify call (packed records): state read,
-    q/k/v/g/beta read, output and record write, qsl + index read."""
+    q/k/v/g/beta read (the raw a/b of the fused-gating form instead, when the
+    workload has them), output and record write, qsl + index read."""
     sa = wl.q.element_size()
     U = wl.units if units is None else units
     T, H, HV, D = wl.tokens, wl.H, wl.HV, wl.D
-    return (U * D * D * 4 + T * H * D * sa * 2 + T * HV * D * sa + T * HV * (4 + wl.beta.element_size())
+    gates = (wl.a.element_size() + wl.b.element_size()) if wl.a is not None else (4 + wl.beta.element_size())
+    return (U * D * D * 4 + T * H * D * sa * 2 + T * HV * D * sa + T * HV * gates
             + T * HV * D * sa + T * HV * (2 * D + 1) * 4 + 8 * wl.B)
 
 
