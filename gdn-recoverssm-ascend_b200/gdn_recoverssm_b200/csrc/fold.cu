@@ -111,15 +111,13 @@ int launch_publish_align(const PublishParams &p, cudaStream_t stream) {
 int launch_compact_conv(const ConvParams &p, int elem_size, cudaStream_t stream) {
   const int64_t grid = p.layers * p.rows;
   const int threads = 256;
-  switch (elem_size) {
-    case 2: compact_conv_kernel<uint16_t><<<static_cast<unsigned>(grid), threads, 0, stream>>>(p); break;
-    case 4: compact_conv_kernel<uint32_t><<<static_cast<unsigned>(grid), threads, 0, stream>>>(p); break;
+  switch (elem_size) {  // a programmatic dependent of the plan, as the fold behind it is of this kernel
+    case 2: return launch_dependent(compact_conv_kernel<uint16_t>, p, static_cast<unsigned>(grid), threads, stream);
+    case 4: return launch_dependent(compact_conv_kernel<uint32_t>, p, static_cast<unsigned>(grid), threads, stream);
     default:
       set_error("GDN RecoverSSM: conv state element size must be 2 or 4 bytes");
       return GDN_RSSM_EUNSUPPORTED;
   }
-  GDN_CUDA(cudaGetLastError());
-  return GDN_RSSM_OK;
 }
 
 }  // namespace gdn_rssm

@@ -104,8 +104,9 @@ __global__ void __launch_bounds__(kFoldThreads, fold_min_blocks<St>()) fold_kern
   const int64_t row = (unit / HV) % p.rows;
   const int64_t layer = unit / (HV * p.rows);
   if (row >= p.record_rows) return;
-  // launched programmatically behind the plan (and, before it, verify): wait
-  // for that grid and its memory before reading plans, records or pages
+  // launched programmatically behind the plan (or the conv compaction behind
+  // it, itself behind the plan): wait for that grid and its memory before
+  // reading plans, records or pages
   ptx::wait_prerequisite_grid();
   const int64_t prow = static_cast<int64_t>(p.layer_groups[layer]) * p.plan_capacity + row;
   if (prow < 0 || prow >= p.plan_len) return;

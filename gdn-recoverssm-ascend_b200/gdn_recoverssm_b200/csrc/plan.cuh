@@ -173,6 +173,8 @@ __global__ void publish_align_kernel(const PublishParams p) {
 // the boundary page may alias the source page).
 template <typename E>
 __global__ void compact_conv_kernel(const ConvParams p) {
+  ptx::wait_prerequisite_grid();  // launched as a dependent of the plan: its results first
+  ptx::launch_dependents();       // the fold may start launching (it waits for this grid)
   const int64_t row = blockIdx.x % p.rows;
   const int64_t layer = blockIdx.x / p.rows;
   const int64_t prow = static_cast<int64_t>(p.layer_groups[layer]) * p.capacity + row;
