@@ -241,6 +241,23 @@ def test_verify_collects_one_native_launch_without_running_it():
     assert len(config) == 28 and config[:8] == [2, 8, 2, 4, 4, 5, 2, 0]
 
 
+def test_empty_batches_return_without_a_launch():
+    """No tokens (or no rows): the output comes back untouched and nothing is
+    launched -- the reference returns early the same way (kernels.py:854-856);
+    CPU tensors prove that no native op ran."""
+    from gdn_recoverssm_b200 import gdn_recoverssm_verify
+
+    kw = _verify_inputs(T=0)
+    kw["query_start_loc"] = torch.zeros(3, dtype=torch.int32)
+    g, beta, q, k, v = (kw.pop(n) for n in ("g", "beta", "q", "k", "v"))
+    out = gdn_recoverssm_verify(g, beta, q, k, v, **kw)
+    assert out.shape == (1, 0, 4, 32)
+    kw = _verify_inputs(T=0)
+    kw.update(query_start_loc=torch.zeros(1, dtype=torch.int32), state_indices=torch.zeros(0, dtype=torch.int32))
+    g, beta, q, k, v = (kw.pop(n) for n in ("g", "beta", "q", "k", "v"))
+    assert gdn_recoverssm_verify(g, beta, q, k, v, **kw).shape == (1, 0, 4, 32)
+
+
 def test_cpu_tensors_fail_loudly_in_the_native_op():
     """No CPU fallback: the op refuses non-CUDA tensors."""
     from gdn_recoverssm_b200 import gdn_recoverssm_verify
