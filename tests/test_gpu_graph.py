@@ -19,14 +19,16 @@ def g():
     return pkg
 
 
-def _step(g, wl, ctx, align_kw):
+def _step(g, wl, ctx, align_kw, conv):
     g.gdn_recoverssm_verify(wl.g, wl.beta, wl.q, wl.k, wl.v, checkpoint_state=wl.state, replay_cache=wl.records,
                             query_start_loc=wl.qsl, state_indices=wl.state_indices, spec_query_len=wl.Q, out=wl.out)
-    ctx.commit(wl.accepted, wl.state_indices, wl.qsl, commit_conv=False, **align_kw)
+    ctx.commit(wl.accepted, wl.state_indices, wl.qsl, commit_conv=conv, **align_kw)
 
 
-@pytest.mark.parametrize("cfg,rows,pool", [(2, 16, 64), (0, None, None)])
-def test_captured_step_replays_bit_exactly(g, cfg, rows, pool):
+@pytest.mark.parametrize("cfg,rows,pool,conv", [(2, 16, 64, False), (2, 16, 64, True), (0, None, None, False)])
+def test_captured_step_replays_bit_exactly(g, cfg, rows, pool, conv):
+    """The plan, conv compaction and fold are programmatic dependents of the
+    kernel before each; captured, they keep those dependencies as graph edges."""
     from gdn_recoverssm_b200 import synthetic
 
     wl = synthetic.make(cfg, "cuda", seed=5, rows=rows, pool=pool, conv_dim=16)
@@ -36,15 +38,16 @@ def test_captured_step_replays_bit_exactly(g, cfg, rows, pool):
                         mamba_block_size=wl.block_size)
     ctx = g.GDNRecoverSSMCommitContext.from_tensors([wl.conv], [wl.state], [wl.records], spec_query_len=wl.Q,
                                                     max_num_reqs=wl.B)
-    state0 = wl.state.clone()
+    state0, conv0 = wl.state.clone(), wl.conv.clone()
 
     # eager
-    _step(g, wl, ctx, align_kw)
+    _step(g, wl, ctx, align_kw, conv)
     torch.cuda.synchronize()
-    eager = (wl.out.clone(), wl.records.clone(), wl.state.clone())
+    eager = (wl.out.clone(), wl.records.clone(), wl.state.clone(), wl.conv.clone())
 
     # captured: restore the inputs, capture once, replay
     wl.state.copy_(state0)
+    wl.conv.copy_(conv0)
     wl.out.zero_()
     wl.records.zero_()
     stream = torch.cuda.Stream()
@@ -52,9 +55,10 @@ def test_captured_step_replays_bit_exactly(g, cfg, rows, pool):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(graph, stream=stream):
-            _step(g, wl, ctx, align_kw)
+            _step(g, wl, ctx, align_kw, conv)
     torch.cuda.current_stream().wait_stream(stream)
     wl.state.copy_(state0)  # capture does not run the kernels, but start from the same pool
+    wl.conv.copy_(conv0)
     wl.out.zero_()
     wl.records.zero_()
     graph.replay()
@@ -62,5 +66,8 @@ def test_captured_step_replays_bit_exactly(g, cfg, rows, pool):
     assert torch.equal(wl.out, eager[0])
     assert torch.equal(wl.records, eager[1])
     assert torch.equal(wl.state, eager[2])
+    assert torch.equal(wl.conv, eager[3])
+    if conv:
+        assert not torch.equal(wl.conv, conv0), "the conv windows were compacted"
     assert int(torch.ops.gdn_recoverssm_ac.device_status()) == 0
     del graph
