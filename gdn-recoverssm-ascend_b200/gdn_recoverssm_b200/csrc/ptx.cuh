@@ -17,6 +17,19 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
 
+// Asynchronous global -> shared copy of 4 or 8 bytes (cp.async, L1-cached);
+// both addresses aligned to the size.  Complete with cp_async_wait_all() in
+// the issuing thread, then a barrier, before others read the destination.
+__device__ __forceinline__ void cp_async_small(void *smem_dst, const void *gsrc, int bytes) {
+  if (bytes == 8) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
+  }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Programmatic dependent launch: a primary kernel lets the next kernel in the
 // stream start launching; that kernel waits for the primary's completion (and
 // its memory) before reading what it wrote.  Both are no-ops without such a

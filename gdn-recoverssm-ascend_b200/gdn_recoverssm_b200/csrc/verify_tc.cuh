@@ -72,6 +72,7 @@ struct VerifyTcShape {
   struct Small {
     uint64_t tile_bar;
     uint64_t mma_bar;
+    uint64_t meta_raw[3];  // bos, eos, slot of the unit two ahead, as copied (cp.async)
     uint32_t tmem;
     float gpart[4][QT * QT];  // Gram partial sums per K slab
     Window win[2];
@@ -243,6 +244,34 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     return tc_unit_meta(bos, eos, slot, QT, p.query_len, p.tokens, p.null_block, p.blocks);
   };
   auto is_live = [&](const TcUnitMeta &m) { return m.slot >= 0; };
+  // The unit two ahead: one thread starts asynchronous copies of its row's raw
+  // qsl / slot entries into shared memory (no registers held, no stall);
+  // everyone decodes them after the next CTA barrier.
+  constexpr int kMetaThread = 64;
+  auto load_meta_async = [&](const TcCursor &c, bool in_range) {  // thread kMetaThread
+    if (!in_range) {
+      sm.meta_raw[0] = 0;
+      sm.meta_raw[1] = 0;
+      sm.meta_raw[2] = ~0ull;  // decodes to slot -1 for either index dtype
+      return;
+    }
+    const int qb = p.qsl_dtype == GDN_RSSM_I64 ? 8 : 4, ib = p.index_dtype == GDN_RSSM_I64 ? 8 : 4;
+    const char *qsl = static_cast<const char *>(p.qsl);
+    const char *idx = static_cast<const char *>(p.indices);
+    ptx::cp_async_small(&sm.meta_raw[0], qsl + static_cast<int64_t>(c.row) * p.qsl_stride * qb, qb);
+    ptx::cp_async_small(&sm.meta_raw[1], qsl + static_cast<int64_t>(c.row + 1) * p.qsl_stride * qb, qb);
+    ptx::cp_async_small(&sm.meta_raw[2], idx + static_cast<int64_t>(c.row) * p.index_stride * ib, ib);
+    ptx::cp_async_commit();
+  };
+  auto decode_meta = [&]() {
+    const uint64_t *raw = sm.meta_raw;
+    auto val = [](uint64_t b, int32_t dt) {
+      return dt == GDN_RSSM_I64 ? static_cast<int64_t>(b)
+                                : static_cast<int64_t>(static_cast<int32_t>(static_cast<uint32_t>(b)));
+    };
+    return tc_unit_meta(val(raw[0], p.qsl_dtype), val(raw[1], p.qsl_dtype), val(raw[2], p.index_dtype), QT,
+                        p.query_len, p.tokens, p.null_block, p.blocks);
+  };
   struct Inputs {  // one unit's activations in registers
     Act x[PER_WARP][EPL];  // q/k: vector warp + 8c, K elements 4 lane .. 4 lane + 3
     Act v[QT];             // v[t][r]
@@ -328,10 +357,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   bool ok = true;
 
   for (int64_t u = blockIdx.x, i = 0; u < units && ok; u += G, ++i) {
-    TcUnitMeta m2;  // two units ahead
-    Inputs in;      // one unit ahead
+    Inputs in;  // one unit ahead
     auto prefetch = [&]() {
-      m2 = load_meta(c2, u + 2 * G < units);
+      if (tid == kMetaThread) load_meta_async(c2, u + 2 * G < units);  // two units ahead
       load_inputs(in, c1, m1);
     };
     const int64_t row = c0.row;
@@ -351,7 +379,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       }
       // the next unit's tile (this unit started none)
       if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
-      __syncthreads();  // the previous unit's recurrence is done with its window buffer
+      if (tid == kMetaThread) ptx::cp_async_wait_all();
+      __syncthreads();  // the previous unit's recurrence is done with its window buffer; metadata copied
     } else {
       // ---- stage the window --------------------------------------------------- //
       // decay and beta of the window -> shared memory (read after the next CTA
@@ -526,6 +555,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           w.A[t] = a;
         }
       }
+      if (tid == kMetaThread) ptx::cp_async_wait_all();  // the copies started a phase ago
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
         if (tid == 0) atomicExch(p.status, kStatusMmaTimeout);
         ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs);
@@ -565,7 +595,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     }
     ic = in;
     m0 = m1;
-    m1 = m2;
+    m1 = decode_meta();  // copied before the last CTA barrier
     c0 = c1;
     c1 = c2;
     c2.advance(dq, dr, HV32);
