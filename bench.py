@@ -165,6 +165,9 @@ def run_reference(args):
         return 0
     from gdn_recoverssm_b200 import synthetic
 
+    # torchrun sets OMP_NUM_THREADS=1 for multi-process launches; rank 0 runs
+    # alone here (the other ranks have exited), so it takes every host core
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     spec = synthetic.CONFIGS[args.config]
     # size each step's sample so that warm-up + K steps fit the time budget
     probe = cpu_baseline(args.config, rows_sample=4, gated=args.gated)
