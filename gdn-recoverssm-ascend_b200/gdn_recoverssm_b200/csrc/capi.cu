@@ -158,7 +158,8 @@ static int verify_impl(const void *q, const void *k, const void *v, const void *
 
   const bool packed = (flags & GDN_RSSM_RECORD_PACKED) != 0;
   const bool normalize = (flags & GDN_RSSM_NORMALIZE_QK) != 0;
-  GDN_REQUIRE((flags & ~(GDN_RSSM_RECORD_PACKED | GDN_RSSM_NORMALIZE_QK)) == 0, "unknown verify flags");
+  GDN_REQUIRE((flags & ~(GDN_RSSM_RECORD_PACKED | GDN_RSSM_NORMALIZE_QK | GDN_RSSM_VERIFY_TEST_NO_TILE)) == 0,
+              "unknown verify flags");
   GDN_REQUIRE(p.null_block == 0, "the null block id must be 0 (page zero is reserved)");
   GDN_REQUIRE(key_dim == value_dim && (key_dim == 32 || key_dim == 64 || key_dim == 128),
               "K and V must be equal and one of 32, 64, 128");

@@ -316,6 +316,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     }
   };
   auto issue_tile = [&](const TcCursor &c, const TcUnitMeta &m) {  // thread 0
+    if (p.flags & GDN_RSSM_VERIFY_TEST_NO_TILE) return;  // failure-detection test: the tile wait runs out
     ptx::mbar_arrive_expect_tx(&sm.tile_bar, Sh::TILE);
 #pragma unroll
     for (int mm = 0; mm < 4; ++mm)  // one 128-row box per 32-column K slab

@@ -76,6 +76,12 @@ enum {
                                      (key = corr + V, decay = corr + V + K; \
                                      the key is per value head)            */
 #define GDN_RSSM_NORMALIZE_QK 2u  /* q,k <- x * rsqrt(sum(x^2) + 1e-6)    */
+/* Test hook for failure detection: the tensor-core verify kernel (K = V = 128,
+ * fp32 pool) starts no state-tile copy, so its bounded wait for the tile runs
+ * out after 1 s; the kernel then records status 1 (copy timeout) in the word
+ * gdn_rssm_device_status() reads, releases its tensor memory and exits, and
+ * the context stays usable.  Ignored by the other kernels. */
+#define GDN_RSSM_VERIFY_TEST_NO_TILE 0x10000u
 
 /* gdn_rssm_fold flags. */
 #define GDN_RSSM_FOLD_PACKED 1u /* records are packed fp32 [R,HV,Q,V+K+1] */
