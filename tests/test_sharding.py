@@ -139,5 +139,46 @@ def test_gloo_world2_sharded_path_reassembles_to_unsharded():
     assert times == [2.0, 10.0]  # MAX over ranks of (rank + 1, 10 - rank)
 
 
+def _failing_rank_main(rank, world, port, result_q):
+    """Rank 1 fails between steps (an exception before the timing reduction);
+    rank 0 must learn of it on the host -- an error from its next collective
+    within the short process-group timeout -- instead of waiting forever."""
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    torch.set_num_threads(1)
+    p = _problem()
+    sh = head_shard(p["q"].shape[1], p["v"].shape[1], world, rank)
+    _run(p, sh.key_begin, sh.key_end, sh.value_begin, sh.value_end)
+    if rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    try:
+        max_over_ranks([1.0])
+        result_q.put("no error")
+    except Exception as exc:  # noqa: BLE001 -- any collective error is the expected outcome
+        result_q.put(f"error: {type(exc).__name__}")
+
+
+def test_gloo_failed_rank_surfaces_as_an_error_on_the_others():
+    world = 2
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_main, args=(r, world, port, result_q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    try:
+        got = result_q.get(timeout=120)
+    finally:
+        for pr in procs:
+            pr.join(timeout=60)
+            if pr.is_alive():
+                pr.kill()
+    assert got.startswith("error"), got
+    assert procs[1].exitcode != 0
+
+
 def test_max_over_ranks_without_process_group_is_identity():
     assert max_over_ranks([1.5, 2.5]) == [1.5, 2.5]
