@@ -224,7 +224,9 @@ def run_b200(args):
     from gdn_recoverssm_b200 import _native, synthetic
 
     _native.ops()
-    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=16, rows=args.rows, pool=args.pool,
+    conv = args.conv_dim > 0
+    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=args.conv_dim if conv else 16,
+                        rows=args.rows, pool=args.pool,
                         gated=args.gated)
     stream = torch.cuda.current_stream(dev)
     ctx = g.GDNRecoverSSMCommitContext.from_tensors([wl.conv], [wl.state], [wl.records], spec_query_len=wl.Q,
@@ -245,8 +247,9 @@ def run_b200(args):
                                     replay_cache=wl.records, query_start_loc=wl.qsl, state_indices=wl.state_indices,
                                     spec_query_len=wl.Q, out=wl.out)
 
-    specs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=False, **align_kw)
+    specs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=conv, **align_kw)
     plan_spec, fold_spec = specs[0], specs[-1]
+    conv_spec = specs[1] if conv else None
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -255,14 +258,14 @@ def run_b200(args):
 
     for _ in range(args.warmup):
         verify()
-        plan_spec.launch()
-        fold_spec.launch()
+        for sp in specs:
+            sp.launch()
     barrier()
     # plan outputs are identical every step (same metadata): byte model inputs
     lens = ctx.commit_lens[: wl.B].cpu()
     bnd = ((ctx.boundary_state_indices[: wl.B] > 0) & (ctx.boundary_recovery_lens[: wl.B] > 0)
            & (ctx.boundary_state_indices[: wl.B] != ctx.final_state_indices[: wl.B])).cpu()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     with ClockSampler(local) as clocks:
         barrier()
         # the step as a serving loop issues it: nothing between the launches
@@ -272,8 +275,8 @@ def run_b200(args):
         t_start.record(stream)
         for i in range(args.steps):
             verify()
-            plan_spec.launch()
-            fold_spec.launch()
+            for sp in specs:  # plan, (conv compaction,) fold
+                sp.launch()
         t_end.record(stream)
         barrier()
         # the same steps again with an event between launches: per-kernel times
@@ -284,20 +287,24 @@ def run_b200(args):
             e[1].record(stream)
             plan_spec.launch()
             e[2].record(stream)
-            fold_spec.launch()
+            if conv_spec is not None:
+                conv_spec.launch()
             e[3].record(stream)
+            fold_spec.launch()
+            e[4].record(stream)
         barrier()
         # end to end through the public API with host buffers
         e2e = _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=args.e2e_buffers)
     total_ms = t_start.elapsed_time(t_end)
     verify_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
     plan_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
-    fold_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
+    conv_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
+    fold_ms = sum(e[3].elapsed_time(e[4]) for e in ev) / args.steps
     step_ms = total_ms / args.steps
     from gdn_recoverssm_b200.sharding import max_over_ranks
 
-    step_ms, verify_ms, plan_ms, fold_ms, e2e_ms = max_over_ranks(
-        [step_ms, verify_ms, plan_ms, fold_ms, e2e["ms"]], device=dev)
+    step_ms, verify_ms, plan_ms, conv_ms, fold_ms, e2e_ms = max_over_ranks(
+        [step_ms, verify_ms, plan_ms, conv_ms, fold_ms, e2e["ms"]], device=dev)
     clk = clocks.summary()
     status = int(torch.ops.gdn_recoverssm_ac.device_status())
     if world > 1:
@@ -310,7 +317,8 @@ def run_b200(args):
     fbytes = synthetic.commit_bytes(wl, lens, int(bnd.sum()))
     fold_gbs = fbytes / (fold_ms * 1e-3) / 1e9
     verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
-    step_gbs = (vbytes + fbytes) / (step_ms * 1e-3) / 1e9
+    cbytes = synthetic.conv_bytes(wl, lens, int(bnd.sum()), ctx.conv_history_len) if conv else 0
+    step_gbs = (vbytes + fbytes + cbytes) / (step_ms * 1e-3) / 1e9
     traffic = _traffic_profile(args.config, args.rows is not None or args.pool is not None)
     if traffic is not None:
         traffic = int(traffic * wl.units / (synthetic.CONFIGS[args.config]["B"] * synthetic.CONFIGS[args.config]["HV"]))
@@ -328,12 +336,16 @@ def run_b200(args):
             "verify": {"ms": verify_ms, "bytes": vbytes, "GB/s": verify_gbs, "frac": verify_gbs / peak},
             "commit_plan": {"ms": plan_ms},
             "fold": {"ms": fold_ms, "bytes": fbytes, "GB/s": fold_gbs, "frac": fold_gbs / peak},
-            "step": {"GB/s": step_gbs, "frac": step_gbs / peak, "per_rank_bytes": vbytes + fbytes},
+            "step": {"GB/s": step_gbs, "frac": step_gbs / peak, "per_rank_bytes": vbytes + fbytes + cbytes},
         },
-        "gpu_launches": 3 * args.steps * world,  # verify, plan, fold per step on every rank
+        "gpu_launches": (4 if conv else 3) * args.steps * world,  # verify, plan, (conv,) fold per step and rank
         "clocks": clk,
         "device_status": status,
     }
+    if conv:
+        conv_gbs = cbytes / (conv_ms * 1e-3) / 1e9
+        line["kernels"]["compact_conv"] = {"ms": conv_ms, "bytes": cbytes, "GB/s": conv_gbs, "frac": conv_gbs / peak}
+        line["config"]["commit_conv"] = f"conv history compacted in the commit: {args.conv_dim} channels"
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(args.config, rows_sample=args.cpu_rows, gated=args.gated)
     print(json.dumps(line))
@@ -403,7 +415,7 @@ def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=3):
                                           use_qk_l2norm_in_kernel=False, **common)
         else:
             g.gdn_recoverssm_verify(d["g"], d["beta"], d["q"], d["k"], d["v"], **common)
-        ctx.commit(d["accepted"], d["state_indices"], d["qsl"], commit_conv=False, **kw)
+        ctx.commit(d["accepted"], d["state_indices"], d["qsl"], commit_conv=args.conv_dim > 0, **kw)
         ev_done[b].record(stream)
         d2h_stream.wait_event(ev_done[b])
         with torch.cuda.stream(d2h_stream):
@@ -439,6 +451,8 @@ def main(argv=None):
     ap.add_argument("--reference-budget-s", type=float, default=60.0,
                     help="CPU seconds the --impl reference run may spend over all its steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--conv-dim", type=int, default=0,
+                    help="also compact the conv history in the commit (channels; 0 = the metric's verify + fold)")
     ap.add_argument("--gated", action="store_true",
                     help="verify through the fused-gating entry point (raw a, b, A_log, dt_bias)")
     ap.add_argument("--e2e-buffers", type=int, default=3, help="device input/output buffers of the end-to-end loop")

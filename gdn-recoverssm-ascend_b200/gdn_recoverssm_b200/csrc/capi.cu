@@ -459,6 +459,9 @@ int gdn_rssm_compact_conv(const int64_t *conv_addrs, const int64_t *conv_block_s
   GDN_REQUIRE(null_block == 0, "the null block id must be 0 (page zero is reserved)");
   GDN_REQUIRE(rows >= 0 && layers > 0 && plan_capacity > 0 && rows <= plan_capacity, "conv geometry");
   GDN_REQUIRE(conv_dim > 0 && history > 0 && window >= history, "conv state is shorter than its window");
+  GDN_REQUIRE(history <= 8, "conv history longer than 8 tokens");
+  GDN_REQUIRE(conv_dim <= int64_t{65535} * 64, "conv state has too many channels");
+  GDN_REQUIRE(window <= 64, "conv state window longer than 64 tokens");
   GDN_REQUIRE(layers * rows < (int64_t(1) << 31), "conv launch grid too large");
   if (rows == 0) return GDN_RSSM_OK;
   GDN_REQUIRE(conv_addrs && conv_block_strides && conv_dim_strides && conv_token_strides && layer_groups && lengths &&

@@ -78,12 +78,12 @@ static unsigned blocks_for(int64_t n, int threads) { return static_cast<unsigned
 // kernel waits in its prologue (griddepcontrol.wait) for that grid's
 // completion and memory, so only the launch latency overlaps.
 template <typename Params>
-static int launch_dependent(void (*kernel)(Params), const Params &p, unsigned grid, unsigned threads,
-                            cudaStream_t stream) {
+static int launch_dependent(void (*kernel)(Params), const Params &p, dim3 grid, unsigned threads,
+                            cudaStream_t stream, unsigned smem = 0) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -108,12 +108,33 @@ int launch_publish_align(const PublishParams &p, cudaStream_t stream) {
   return GDN_RSSM_OK;
 }
 
-int launch_compact_conv(const ConvParams &p, int elem_size, cudaStream_t stream) {
-  const int64_t grid = p.layers * p.rows;
-  const int threads = 256;
+int launch_compact_conv(const ConvParams &params, int elem_size, cudaStream_t stream) {
+  ConvParams p = params;
+  // chunk of channels per CTA: the largest that lets the contiguous path
+  // stage three chunks in the default 48 KB of shared memory
+  p.chunk = kConvChannelsPerCta;
+  const int64_t row_bytes = p.window * elem_size;
+  while (p.chunk > 64 && 3 * p.chunk * row_bytes > kConvSmemLimit) p.chunk /= 2;
+  p.vec = (3 * p.chunk * row_bytes <= kConvSmemLimit && (p.chunk * row_bytes) % 16 == 0) ? 1 : 0;
+  const unsigned smem = p.vec ? static_cast<unsigned>(3 * p.chunk * row_bytes) : 0u;
+  // x: (layer, row); y: chunks of channels
+  const dim3 grid(static_cast<unsigned>(p.layers * p.rows), static_cast<unsigned>((p.conv_dim + p.chunk - 1) / p.chunk));
+  static bool carveout[2][64] = {};  // shared memory first: six 36 KB CTAs per SM, not three
+  int dev = 0;
+  GDN_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && (elem_size == 2 || elem_size == 4) && !carveout[elem_size / 4][dev]) {
+    if (elem_size == 2) {
+      GDN_CUDA(cudaFuncSetAttribute(compact_conv_kernel<uint16_t>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared));
+    } else {
+      GDN_CUDA(cudaFuncSetAttribute(compact_conv_kernel<uint32_t>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared));
+    }
+    carveout[elem_size / 4][dev] = true;
+  }
   switch (elem_size) {  // a programmatic dependent of the plan, as the fold behind it is of this kernel
-    case 2: return launch_dependent(compact_conv_kernel<uint16_t>, p, static_cast<unsigned>(grid), threads, stream);
-    case 4: return launch_dependent(compact_conv_kernel<uint32_t>, p, static_cast<unsigned>(grid), threads, stream);
+    case 2: return launch_dependent(compact_conv_kernel<uint16_t>, p, grid, kConvThreads, stream, smem);
+    case 4: return launch_dependent(compact_conv_kernel<uint32_t>, p, grid, kConvThreads, stream, smem);
     default:
       set_error("GDN RecoverSSM: conv state element size must be 2 or 4 bytes");
       return GDN_RSSM_EUNSUPPORTED;

@@ -20,6 +20,13 @@
 
 namespace gdn_rssm {
 
+// Longest conv history compacted (kernel width - 1; the Gated DeltaNet family
+// uses width 4, history 3).
+constexpr int kMaxConvHistory = 8;
+constexpr int kConvThreads = 256;
+constexpr int kConvChannelsPerCta = 1024;  // largest chunk
+constexpr int kConvSmemLimit = 48 * 1024;  // staging of the contiguous path: 3 chunks
+
 
 __global__ void commit_plan_kernel(const CommitPlanParams p) {
   // launched as a programmatic dependent of the kernel before it (the sampler
@@ -172,7 +179,7 @@ __global__ void publish_align_kernel(const PublishParams p) {
 // Both windows are read into registers before either is stored (the final or
 // the boundary page may alias the source page).
 template <typename E>
-__global__ void compact_conv_kernel(const ConvParams p) {
+__global__ void __launch_bounds__(kConvThreads, 6) compact_conv_kernel(const ConvParams p) {
   ptx::wait_prerequisite_grid();  // launched as a dependent of the plan: its results first
   ptx::launch_dependents();       // the fold may start launching (it waits for this grid)
   const int64_t row = blockIdx.x % p.rows;
@@ -194,19 +201,78 @@ __global__ void compact_conv_kernel(const ConvParams p) {
   E *base = reinterpret_cast<E *>(p.addrs[layer]);
   const int64_t bs = p.block_strides[layer], ds = p.dim_strides[layer], ts = p.token_strides[layer];
   const E *srcp = base + src * bs;
-  const int64_t total = p.conv_dim * p.history;
-  // The kernel's own footprint is bounded by what one CTA holds per pass.
-  for (int64_t i0 = 0; i0 < total; i0 += blockDim.x) {
-    const int64_t i = i0 + threadIdx.x;
-    const bool live = i < total;
-    const int64_t d = live ? i / p.history : 0, hh = live ? i % p.history : 0;
-    E fv{}, bv{};
-    if (live) fv = srcp[d * ds + (n - 1 + hh) * ts];
-    if (live && do_b) bv = srcp[d * ds + (blen - 1 + hh) * ts];
-    __syncthreads();  // every read of this pass precedes every store of it
-    if (live && do_b) base[bidx * bs + d * ds + hh * ts] = bv;
-    if (live) base[fin * bs + d * ds + hh * ts] = fv;
+  E *finp = base + fin * bs;
+  E *bndp = base + (do_b ? bidx : 0) * bs;
+  const int hist = static_cast<int>(p.history);  // <= kMaxConvHistory (checked on the host)
+  const int64_t d0 = static_cast<int64_t>(blockIdx.y) * p.chunk;
+  const int64_t nch = p.conv_dim - d0 < p.chunk ? p.conv_dim - d0 : p.chunk;
+  if (nch <= 0) return;
+  const int64_t W = p.window;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(srcp + d0 * W) | reinterpret_cast<uintptr_t>(finp + d0 * W) |
+                         reinterpret_cast<uintptr_t>(bndp + d0 * W)) & 15) == 0;
+  if (p.vec && ts == 1 && ds == W && aligned) {
+    // Contiguous windows: the chunk's rows of the source, final and boundary
+    // pages come into shared memory with 16-byte copies, the history windows
+    // move there, and the final / boundary chunks go back whole -- full-sector
+    // traffic instead of 2-byte accesses.  Every read precedes every store,
+    // so pages that alias (in place, boundary == source) behave as above.
+    extern __shared__ __align__(16) unsigned char conv_smem[];
+    E *sA = reinterpret_cast<E *>(conv_smem);
+    E *sB = sA + static_cast<int64_t>(p.chunk) * W;
+    E *sC = sB + static_cast<int64_t>(p.chunk) * W;
+    const int64_t elems = nch * W;
+    const int64_t nvec = elems * static_cast<int64_t>(sizeof(E)) / 16;
+    const int64_t tail0 = nvec * 16 / static_cast<int64_t>(sizeof(E));
+    auto copy_in = [&](E *dst, const E *src) {  // asynchronous 16-byte copies (cp.async), no register round trip
+      for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x)
+        ptx::cp_async16(reinterpret_cast<uint4 *>(dst) + i, reinterpret_cast<const uint4 *>(src) + i);
+      for (int64_t i = tail0 + threadIdx.x; i < elems; i += blockDim.x) dst[i] = src[i];
+    };
+    auto copy_out = [&](E *dst, const E *src) {
+      for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x)
+        reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
+      for (int64_t i = tail0 + threadIdx.x; i < elems; i += blockDim.x) dst[i] = src[i];
+    };
+    copy_in(sA, srcp + d0 * W);
+    copy_in(sB, finp + d0 * W);
+    if (do_b) copy_in(sC, bndp + d0 * W);
+    ptx::cp_async_commit();
+    ptx::cp_async_wait_all();
     __syncthreads();
+    for (int64_t c = threadIdx.x; c < nch; c += blockDim.x) {
+      const E *a = sA + c * W;
+      for (int h = 0; h < hist; ++h) {
+        sB[c * W + h] = a[n - 1 + h];
+        if (do_b) sC[c * W + h] = a[blen - 1 + h];
+      }
+    }
+    __syncthreads();
+    if (do_b) copy_out(bndp + d0 * W, sC);  // same thread per address as the final copy: final lands last
+    copy_out(finp + d0 * W, sB);
+    return;
+  }
+  // General strides: one thread per channel; it reads both windows of its
+  // channel before it stores either (boundary first, then final), and no two
+  // threads touch the same channel, so an in-place row (final or boundary ==
+  // source) needs no barrier.
+  for (int64_t d = d0 + threadIdx.x; d < d0 + nch; d += blockDim.x) {
+    const E *sd = srcp + d * ds;
+    E fv[kMaxConvHistory], bv[kMaxConvHistory];
+#pragma unroll
+    for (int h = 0; h < kMaxConvHistory; ++h) {
+      if (h < hist) {
+        fv[h] = sd[(n - 1 + h) * ts];
+        if (do_b) bv[h] = sd[(blen - 1 + h) * ts];
+      }
+    }
+    if (do_b) {
+#pragma unroll
+      for (int h = 0; h < kMaxConvHistory; ++h)
+        if (h < hist) bndp[d * ds + h * ts] = bv[h];
+    }
+#pragma unroll
+    for (int h = 0; h < kMaxConvHistory; ++h)
+      if (h < hist) finp[d * ds + h * ts] = fv[h];
   }
 }
 

@@ -218,6 +218,15 @@ def verify_bytes(wl: Workload, units: int | None = None) -> int:
             + T * HV * D * sa + T * HV * (2 * D + 1) * 4 + 8 * wl.B)
 
 
+def conv_bytes(wl: Workload, lengths, boundary_written, history: int) -> int:
+    """Algorithmic bytes of one conv compaction: per working row the history
+    window read and written (twice where a boundary snapshot is also taken)."""
+    n = torch.as_tensor(lengths).long()
+    working = int((n > 0).sum())
+    per = wl.conv.shape[1] * history * wl.conv.element_size() * 2
+    return (working + int(boundary_written)) * per
+
+
 def commit_bytes(wl: Workload, lengths, boundary_written) -> int:
     """Algorithmic bytes of one fold call: state read + final write (+ the
     boundary snapshot where one is written) + the accepted records read."""
