@@ -220,18 +220,21 @@ __global__ void __launch_bounds__(kConvThreads, 6) compact_conv_kernel(const Con
     E *sA = reinterpret_cast<E *>(conv_smem);
     E *sB = sA + static_cast<int64_t>(p.chunk) * W;
     E *sC = sB + static_cast<int64_t>(p.chunk) * W;
-    const int64_t elems = nch * W;
-    const int64_t nvec = elems * static_cast<int64_t>(sizeof(E)) / 16;
-    const int64_t tail0 = nvec * 16 / static_cast<int64_t>(sizeof(E));
+    // 32-bit indices inside a chunk (at most 48 KB of shared memory)
+    const int w = static_cast<int>(W), nc = static_cast<int>(nch);
+    const int elems = nc * w;
+    const int nvec = elems * static_cast<int>(sizeof(E)) / 16;
+    const int tail0 = nvec * 16 / static_cast<int>(sizeof(E));
+    const int tid = threadIdx.x;
     auto copy_in = [&](E *dst, const E *src) {  // asynchronous 16-byte copies (cp.async), no register round trip
-      for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x)
+      for (int i = tid; i < nvec; i += kConvThreads)
         ptx::cp_async16(reinterpret_cast<uint4 *>(dst) + i, reinterpret_cast<const uint4 *>(src) + i);
-      for (int64_t i = tail0 + threadIdx.x; i < elems; i += blockDim.x) dst[i] = src[i];
+      for (int i = tail0 + tid; i < elems; i += kConvThreads) dst[i] = src[i];
     };
     auto copy_out = [&](E *dst, const E *src) {
-      for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x)
+      for (int i = tid; i < nvec; i += kConvThreads)
         reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
-      for (int64_t i = tail0 + threadIdx.x; i < elems; i += blockDim.x) dst[i] = src[i];
+      for (int i = tail0 + tid; i < elems; i += kConvThreads) dst[i] = src[i];
     };
     copy_in(sA, srcp + d0 * W);
     copy_in(sB, finp + d0 * W);
@@ -239,11 +242,13 @@ __global__ void __launch_bounds__(kConvThreads, 6) compact_conv_kernel(const Con
     ptx::cp_async_commit();
     ptx::cp_async_wait_all();
     __syncthreads();
-    for (int64_t c = threadIdx.x; c < nch; c += blockDim.x) {
-      const E *a = sA + c * W;
-      for (int h = 0; h < hist; ++h) {
-        sB[c * W + h] = a[n - 1 + h];
-        if (do_b) sC[c * W + h] = a[blen - 1 + h];
+    for (int c = tid; c < nc; c += kConvThreads) {
+      const E *a = sA + c * w;
+      E *b = sB + c * w;
+      for (int h = 0; h < hist; ++h) b[h] = a[n - 1 + h];
+      if (do_b) {
+        E *cc = sC + c * w;
+        for (int h = 0; h < hist; ++h) cc[h] = a[blen - 1 + h];
       }
     }
     __syncthreads();
