@@ -20,16 +20,19 @@
 //
 // Grid: up to three CTAs (256 threads) per SM (two at Q = 8), each walking the
 // units blockIdx.x, blockIdx.x + gridDim.x, ...; per unit:
-//   all:      stage [hi(X); lo(X)], g / beta, decay and key records (the
-//             unit's q/k/v/g/beta were loaded into registers during the
-//             previous unit); wait for the tile;
+//   all:      stage [hi(X); lo(X)], decay / beta and the decay and key
+//             records (the unit's q/k/v/g/beta were loaded into registers
+//             during the previous unit); wait for the tile;
 //   thread 0: pass 1, no commit yet;
 //   all:      meanwhile bf16(lo(S)) -> tensor memory (one row per lane),
-//             bf16(X) -> the pass-2 operand, the Gram partial sums, the loads
-//             of the next units' slots and activations;
+//             bf16(X) -> the pass-2 operand; warps 4-7 the Gram partial
+//             sums; the loads of the next unit's activations, and one
+//             thread's cp.async of the row metadata of the unit after it into
+//             shared memory; with the fused gating prologue, warp 1 computes
+//             decay / beta from the raw inputs here;
 //   thread 0: pass 2 right behind pass 1, one commit for both;
-//   warps 4+: Gram coefficients (warp 0, which issues the MMAs, does none of
-//             the per-unit scalar work); after the commit, thread 0 starts the NEXT
+//   warps 4+: Gram coefficients (warp 0, which issues the MMAs, takes no
+//             part in the Gram); after the commit, thread 0 starts the NEXT
 //             unit's tile (4-D tensor map, 128-byte swizzle -- the layout
 //             the MMA's K-major descriptor reads directly -- one 128-row box
 //             per K slab) into the freed buffer, and every warp loads its 32
