@@ -166,3 +166,35 @@ def test_gated_equals_ungated_with_host_gates(pkg):
     ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(o1), 1e-30))) - 7)
     assert np.all((np.abs(o0 - o1) <= ulp * 1.01) | (np.abs(o0 - o1) <= 1e-5 * vmax)), "outputs"
     assert int(torch.ops.gdn_recoverssm_ac.device_status()) == 0
+
+
+def test_capi_gated_direct_call_matches_torch_op(pkg):
+    """gdn_rssm_verify_gated called through ctypes with raw device pointers
+    (the binding a non-torch host would use) gives bit-identical results to
+    the torch op."""
+    from gdn_recoverssm_b200 import capi
+
+    D, Q, HV, H = 128, 4, 4, 2
+    c = _inputs(91, D, Q, torch.bfloat16, torch.bfloat16, H, HV, True)
+    dev = {n: x.cuda() for n, x in c.items()}
+    T, rows = c["q"].shape[0], c["slots"].shape[0]
+    res = []
+    for direct in (False, True):
+        out = torch.zeros(1, T, HV, D, dtype=torch.bfloat16, device="cuda")
+        cache = torch.zeros(rows, HV, Q, 2 * D + 1, device="cuda")
+        specs = []
+        pkg.gdn_recoverssm_verify_gated(dev["A_log"], dev["a"], dev["b"], dev["dt_bias"], dev["q"][None],
+                                        dev["k"][None], dev["v"][None], checkpoint_state=dev["state"],
+                                        replay_cache=cache, query_start_loc=dev["qsl"], state_indices=dev["slots"],
+                                        spec_query_len=Q, out=out, _collect=specs)
+        (q, k, v, a, b, A_log, dt_bias, state, corr, key, decay, o, qsl, idx, config, scale, sb, thr,
+         flags) = specs[0].args
+        if direct:
+            capi.verify_gated(q, k, v, a, b, A_log, dt_bias, state, corr, key, decay, o, qsl, idx, config, scale, sb,
+                              thr, flags=flags)
+        else:
+            specs[0].launch()
+        torch.cuda.synchronize()
+        res.append((out.cpu(), cache.cpu()))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+    assert int(torch.ops.gdn_recoverssm_ac.device_status()) == 0
