@@ -370,3 +370,31 @@ def test_coordinator_buckets_and_publication_counts(monkeypatch):
     bad[1].payload.block_size = 8
     with pytest.raises(ValueError, match="must agree"):
         coord.commit([e.metadata for e in bad], *_inputs())
+
+
+def test_algorithmic_byte_model_matches_the_survey_formula():
+    """The roofline's byte counts (synthetic.verify_bytes / commit_bytes /
+    conv_bytes) at config 2: U*V*K*4 + T*H*K*2*2 + T*HV*V*2 + T*HV*(4+4) +
+    T*HV*V*2 + T*HV*(V+K+1)*4 + 8*B for verify; the fold's read + write of
+    every working unit, boundary snapshots and accepted records."""
+    from types import SimpleNamespace
+
+    from gdn_recoverssm_b200 import synthetic
+
+    B, H, HV, D, Q = 512, 16, 32, 128, 4
+    T = B * Q
+    act = torch.empty(0, dtype=torch.bfloat16)
+    wl = SimpleNamespace(B=B, H=H, HV=HV, D=D, Q=Q, tokens=T, units=B * HV, q=act, a=None,
+                         beta=torch.empty(0, dtype=torch.float32),
+                         conv=torch.empty(1, 8192, 6, dtype=torch.bfloat16))
+    want = (B * HV * D * D * 4 + T * H * D * 2 * 2 + T * HV * D * 2 + T * HV * 8 + T * HV * D * 2
+            + T * HV * (2 * D + 1) * 4 + 8 * B)
+    assert synthetic.verify_bytes(wl) == want == 1191972864
+    lens = torch.tensor([4, 0, 2, 1] * (B // 4))
+    working = int((lens > 0).sum())
+    fold = working * HV * D * D * 4 * 2 + 3 * HV * D * D * 4 + int(lens.sum()) * HV * (2 * D + 1) * 4 + 24 * B
+    assert synthetic.commit_bytes(wl, lens, 3) == fold
+    assert synthetic.conv_bytes(wl, lens, 3, 3) == (working + 3) * 8192 * 3 * 2 * 2
+    wl.a = act  # fused gating: raw a, b in the activation dtype instead of g, beta
+    wl.b = act
+    assert synthetic.verify_bytes(wl) == want - T * HV * 4
