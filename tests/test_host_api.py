@@ -138,6 +138,25 @@ def test_capi_fold_and_plans_reject_before_launch():
     assert rc == capi.EINVAL and "window" in capi.last_error()
 
 
+@pytest.mark.parametrize(
+    "conv_dim,history,window,match",
+    [
+        (16, 9, 12, "conv history longer than 8 tokens"),
+        (16, 3, 65, "window longer than 64"),
+        (65535 * 64 + 1, 3, 6, "too many channels"),
+        (16, 0, 6, "shorter than its window"),
+    ],
+)
+def test_capi_compact_conv_rejects_geometry(conv_dim, history, window, match):
+    from gdn_recoverssm_b200 import capi
+
+    lib = capi.lib()
+    # plan_len, rows, layers, capacity, conv_dim, history, window, num_blocks, null, dtype, align
+    rc = lib.gdn_rssm_compact_conv(*([None] * 5), capi.index_view(None), *([None] * 4), 8, 2, 1, 4, conv_dim,
+                                   history, window, 8, 0, capi.BF16, 1, None)
+    assert rc == capi.EINVAL and match in capi.last_error()
+
+
 # ---- Python entry points -------------------------------------------------- #
 def test_record_geometry_bytes_matches_reference_deployment():
     from gdn_recoverssm_b200 import kernels
