@@ -61,6 +61,10 @@ def _verify_call(lib, capi, config, **over):
                                args["key"], args["qsl"], args["idx"], args["K"], args["V"], args["flags"], None)
 
 
+def capi_flags_unknown():
+    return 1 << 20  # not a verify flag (GDN_RSSM_VERIFY_TEST_NO_TILE is 1 << 16)
+
+
 def _good_config():
     # rows, tokens, H, HV, Q, blocks, record_rows, null, ... strides
     return [4, 16, 2, 4, 4, 8, 4, 0] + [1] * 20
@@ -79,6 +83,9 @@ def _good_config():
         (lambda c: c, {"flags": 0, "key": 1, "act": 0}, "low-precision key"),
         (lambda c: c, {"state": 2}, "state must be"),
         (lambda c: c[:1] + [100] + c[2:], {}, "activation capacity"),
+        (lambda c: [2**31, 2**31] + c[2:], {}, "below 2^31"),
+        (lambda c: c[:5] + [2**31] + c[6:], {}, "below 2^31"),
+        (lambda c: c, {"flags": capi_flags_unknown()}, "unknown verify flags"),
     ],
 )
 def test_capi_verify_rejects_before_launch(mutate, over, match):
