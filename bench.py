@@ -2,10 +2,18 @@
 
 One step = one speculative verify over a batch (gdn_recoverssm_verify) plus the
 commit of the accepted prefixes (GDNRecoverSSMCommitContext.commit: plan +
-fold, conv compaction excluded as in the byte model) on one GDN layer of the
-named configuration (default: config 2, B=512, H=16, HV=32, K=V=128, Q=4,
-prefix-cache align mode with 64-token blocks, bf16 q/k/v, fp32 state pool of
-4096 pages, packed fp32 records).  Synthetic, seeded inputs of those shapes.
+fold; `--conv-dim D` adds the conv compaction of D channels) on one GDN layer
+of the named configuration (default: config 2, B=512, H=16, HV=32, K=V=128,
+Q=4, prefix-cache align mode with 64-token blocks, bf16 q/k/v, fp32 state pool
+of 4096 pages, packed fp32 records).  Synthetic, seeded inputs of those
+shapes.  `--gated` verifies through the fused-gating entry point.
+
+The headline loop issues the steps back to back with nothing between the
+launches; a second pass with CUDA events between the launches gives the
+per-kernel split.  `e2e` repeats the step through the public API with the
+inputs copied from pinned host memory and the output copied back, every step.
+`--impl reference` times the CPU restatement of the reference's path
+(oracle/cpu_executors.py) on the host cores instead.
 
 Multi-GPU (torchrun, one process per GPU): value heads (and their key heads)
 are sharded across ranks, each rank owning the state pool of its heads; the
@@ -13,6 +21,7 @@ launches are independent, with no collective in the path (host barrier and a
 MAX reduction of the timings only, outside the timed region).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl b200|reference]
+                    [--gated] [--conv-dim D] [--no-cpu-baseline]
 """
 
 from __future__ import annotations
