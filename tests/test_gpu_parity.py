@@ -268,3 +268,46 @@ def test_op_rejects_bad_arguments_before_launch(pkg):
         ops.verify_ext(_dev(c["q"])[None], _dev(c["k"])[None], _dev(c["v"])[None], _dev(c["g"]), _dev(c["beta"]),
                        _dev(c["state"]), bad, bad, bad, bad, _dev(c["qsl"]), _dev(c["state_indices"]),
                        [0] * 28, 1.0, 1)
+
+
+def test_reference_schema_ops_match_the_extended_ops(pkg):
+    """The drop-ins for the reference's native ops -- gdn_recoverssm_ac::verify
+    and ::fold with their exact schemas (typed records, no flags; what the
+    reference's AscendC backend calls) -- give bit-identical results to the
+    extended ops the Python layer launches."""
+    from gdn_recoverssm_b200 import synthetic
+
+    g = pkg
+    ops = torch.ops.gdn_recoverssm_ac
+    wl = synthetic.make(1, "cuda", seed=21, rows=8, pool=32, conv_dim=8)
+    H, HV, D, Q, B = wl.H, wl.HV, wl.D, wl.Q, wl.B
+    results = []
+    for reference_schema in (False, True):
+        state = wl.state.clone()
+        rec = g.ReplayRecordBuffers.allocate(B, HV, H, Q, D, D, device="cuda", key_dtype=wl.k.dtype)
+        out = torch.zeros_like(wl.out)
+        specs = []
+        g.gdn_recoverssm_verify(wl.g, wl.beta, wl.q, wl.k, wl.v, checkpoint_state=state, replay_cache=rec,
+                                query_start_loc=wl.qsl, state_indices=wl.state_indices, spec_query_len=Q, out=out,
+                                _collect=specs)
+        (spec,) = specs
+        assert spec.args[-1] == 0  # typed records, pre-normalised q/k: the reference's own op applies
+        if reference_schema:
+            ops.verify(*spec.args[:-1])
+        else:
+            spec.launch()
+        conv = torch.zeros(wl.state.shape[0], 8, 3 + Q - 1, dtype=wl.q.dtype, device="cuda")
+        ctx = g.GDNRecoverSSMCommitContext.from_tensors([conv], [state], [rec], spec_query_len=Q, max_num_reqs=B)
+        cspecs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=False)
+        plan, fold = cspecs[0], cspecs[-1]
+        plan.launch()
+        assert fold.args[-1] == 0
+        if reference_schema:
+            ops.fold(*fold.args[:-1])
+        else:
+            fold.launch()
+        torch.cuda.synchronize()
+        results.append((out.cpu(), rec.correction.cpu(), rec.key.cpu(), rec.decay.cpu(), state.cpu()))
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+    assert int(ops.device_status()) == 0
