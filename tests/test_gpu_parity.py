@@ -270,24 +270,27 @@ def test_op_rejects_bad_arguments_before_launch(pkg):
                        [0] * 28, 1.0, 1)
 
 
-def test_reference_schema_ops_match_the_extended_ops(pkg):
+@pytest.mark.parametrize("act", [torch.bfloat16, torch.float16])
+def test_reference_schema_ops_match_the_extended_ops(pkg, act):
     """The drop-ins for the reference's native ops -- gdn_recoverssm_ac::verify
     and ::fold with their exact schemas (typed records, no flags; what the
     reference's AscendC backend calls) -- give bit-identical results to the
-    extended ops the Python layer launches."""
+    extended ops the Python layer launches; the fold of typed records with
+    bf16 / fp16 key planes matches the float64 oracle."""
     from gdn_recoverssm_b200 import synthetic
 
     g = pkg
     ops = torch.ops.gdn_recoverssm_ac
     wl = synthetic.make(1, "cuda", seed=21, rows=8, pool=32, conv_dim=8)
+    q, k, v = wl.q.to(act), wl.k.to(act), wl.v.to(act)
     H, HV, D, Q, B = wl.H, wl.HV, wl.D, wl.Q, wl.B
     results = []
     for reference_schema in (False, True):
         state = wl.state.clone()
-        rec = g.ReplayRecordBuffers.allocate(B, HV, H, Q, D, D, device="cuda", key_dtype=wl.k.dtype)
-        out = torch.zeros_like(wl.out)
+        rec = g.ReplayRecordBuffers.allocate(B, HV, H, Q, D, D, device="cuda", key_dtype=act)
+        out = torch.zeros(wl.out.shape, dtype=act, device="cuda")
         specs = []
-        g.gdn_recoverssm_verify(wl.g, wl.beta, wl.q, wl.k, wl.v, checkpoint_state=state, replay_cache=rec,
+        g.gdn_recoverssm_verify(wl.g, wl.beta, q, k, v, checkpoint_state=state, replay_cache=rec,
                                 query_start_loc=wl.qsl, state_indices=wl.state_indices, spec_query_len=Q, out=out,
                                 _collect=specs)
         (spec,) = specs
@@ -296,7 +299,7 @@ def test_reference_schema_ops_match_the_extended_ops(pkg):
             ops.verify(*spec.args[:-1])
         else:
             spec.launch()
-        conv = torch.zeros(wl.state.shape[0], 8, 3 + Q - 1, dtype=wl.q.dtype, device="cuda")
+        conv = torch.zeros(wl.state.shape[0], 8, 3 + Q - 1, dtype=act, device="cuda")
         ctx = g.GDNRecoverSSMCommitContext.from_tensors([conv], [state], [rec], spec_query_len=Q, max_num_reqs=B)
         cspecs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=False)
         plan, fold = cspecs[0], cspecs[-1]
@@ -311,3 +314,12 @@ def test_reference_schema_ops_match_the_extended_ops(pkg):
     for a, b in zip(*results):
         assert torch.equal(a, b)
     assert int(ops.device_status()) == 0
+    # the fold of the typed records (key planes in the activation dtype) against the oracle
+    _, corr, key, decay, got = results[1]
+    want = [wl.state.double().cpu().numpy()]
+    O.fold(want, [corr.numpy()], [key.float().numpy()], [decay.numpy()], layer_groups=[0],
+           plan_capacity=ctx.commit_lens.shape[0], rows=B, source=wl.state_indices.cpu().numpy(),
+           lengths=ctx.commit_lens.cpu().numpy(), finals=ctx.final_state_indices.cpu().numpy(),
+           boundaries=ctx.boundary_state_indices.cpu().numpy(), boundary_lens=ctx.boundary_recovery_lens.cpu().numpy(),
+           num_blocks=wl.state.shape[0], record_rows=B, layout="soa", query_len=Q)
+    assert_fp32_close(got.double().numpy(), want[0], what="typed-record fold")
