@@ -36,6 +36,8 @@ SUPPORTED_HEAD_DIMS = (32, 64, 128)
 # flags of the extended native ops (include/gdn_recoverssm_b200.h)
 _RECORD_PACKED = 1
 _NORMALIZE_QK = 2
+_ACT_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+_INDEX_DTYPES = (torch.int32, torch.int64)
 _FOLD_PACKED = 1
 
 
@@ -236,41 +238,52 @@ def _verify(g, beta, q, k, v, checkpoint_state, replay_cache, query_start_loc, s
             qk_already_normalized, out, _collect, gate):
     """Shared validation and launch of both verify forms; ``gate`` is
     ``(A_log, dt_bias, softplus_beta, softplus_threshold)`` for the fused
-    gating form (``g`` / ``beta`` then carry the raw ``a`` / ``b``)."""
-    _require(q.ndim == 4 and q.shape[0] == 1, "q must have shape [1, tokens, heads, dim]")
-    _, total, H, K = q.shape
-    _require(k.shape == q.shape, "q and k shapes differ")
-    _require(v.ndim == 4 and tuple(v.shape[:2]) == (1, total), "v must have shape [1, tokens, value heads, dim]")
-    HV, V = v.shape[-2], v.shape[-1]
+    gating form (``g`` / ``beta`` then carry the raw ``a`` / ``b``).
+
+    Every shape and stride tuple is read once: the checks run on every decode
+    step, so their host cost is per-step latency."""
+    qshape = q.shape
+    _require(len(qshape) == 4 and qshape[0] == 1, "q must have shape [1, tokens, heads, dim]")
+    _, total, H, K = qshape
+    _require(k.shape == qshape, "q and k shapes differ")
+    vshape = v.shape
+    _require(len(vshape) == 4 and vshape[0] == 1 and vshape[1] == total,
+             "v must have shape [1, tokens, value heads, dim]")
+    HV, V = vshape[2], vshape[3]
     _require(H > 0 and HV >= H and HV % H == 0, "value heads must be a positive multiple of the q/k heads")
     _require(g.numel() == total * HV and beta.numel() == total * HV, "gate or beta shape is incompatible")
     g2 = g.reshape(total, HV)
     beta2 = beta.reshape(total, HV)
-    _require(g2.stride(1) == 1 and beta2.stride(1) == 1, "gate and beta heads must be contiguous")
+    gs, bs = g2.stride(), beta2.stride()
+    _require(gs[1] == 1 and bs[1] == 1, "gate and beta heads must be contiguous")
     _require(0 < spec_query_len <= MAX_SPEC_QUERY_LEN, f"spec_query_len must be in [1, {MAX_SPEC_QUERY_LEN}]")
-    _require(all(t_.stride(-1) == 1 and t_.stride(-2) == K for t_ in (q, k)), "q and k heads must be contiguous")
-    _require(v.stride(-1) == 1 and v.stride(-2) == V, "v heads must be contiguous")
-    _require(checkpoint_state.ndim == 4, "checkpoint must be four-dimensional")
-    nb = checkpoint_state.shape[0]
-    _require(tuple(checkpoint_state.shape[1:]) == (HV, V, K), "checkpoint shape is incompatible")
+    qs, ks, vs = q.stride(), k.stride(), v.stride()
+    _require(qs[3] == 1 and qs[2] == K and ks[3] == 1 and ks[2] == K, "q and k heads must be contiguous")
+    _require(vs[3] == 1 and vs[2] == V, "v heads must be contiguous")
+    cshape = checkpoint_state.shape
+    _require(len(cshape) == 4, "checkpoint must be four-dimensional")
+    nb = cshape[0]
+    _require(cshape[1] == HV and cshape[2] == V and cshape[3] == K, "checkpoint shape is incompatible")
     _require(K == V and K in SUPPORTED_HEAD_DIMS, f"K and V must be equal and one of {SUPPORTED_HEAD_DIMS}")
+    qdt = q.dtype
     if gate is None:
         _require(g2.dtype == torch.float32, "gate must be FP32 log-space decay")
     else:
-        _require(g2.dtype in (torch.float32, q.dtype), "a must be FP32 or the activation dtype")
-    _require(beta2.dtype in (torch.float32, q.dtype), "beta must be FP32 or the activation dtype")
-    _require(q.dtype in (torch.float32, torch.bfloat16, torch.float16) and k.dtype == q.dtype and v.dtype == q.dtype,
-             "q/k/v must share one FP32/BF16/FP16 dtype")
-    _require(checkpoint_state.dtype == torch.float32 or (checkpoint_state.dtype == torch.bfloat16 and K >= 64),
+        _require(g2.dtype in (torch.float32, qdt), "a must be FP32 or the activation dtype")
+    _require(beta2.dtype in (torch.float32, qdt), "beta must be FP32 or the activation dtype")
+    _require(qdt in _ACT_DTYPES and k.dtype == qdt and v.dtype == qdt, "q/k/v must share one FP32/BF16/FP16 dtype")
+    cdt = checkpoint_state.dtype
+    _require(cdt == torch.float32 or (cdt == torch.bfloat16 and K >= 64),
              "checkpoint must be FP32 (or BF16 with K >= 64)")
     soa = isinstance(replay_cache, ReplayRecordBuffers)
     if soa:
         corr, key_record, decay_record = replay_cache.correction, replay_cache.key, replay_cache.decay
+        rshape = corr.shape
         _require(
-            corr.ndim == 4
-            and tuple(corr.shape[1:]) == (HV, spec_query_len, V)
-            and tuple(key_record.shape) == (corr.shape[0], H, spec_query_len, K)
-            and tuple(decay_record.shape) == (corr.shape[0], HV, spec_query_len),
+            len(rshape) == 4
+            and tuple(rshape[1:]) == (HV, spec_query_len, V)
+            and tuple(key_record.shape) == (rshape[0], H, spec_query_len, K)
+            and tuple(decay_record.shape) == (rshape[0], HV, spec_query_len),
             "typed record geometry is incompatible",
         )
         _require(corr.dtype == decay_record.dtype == torch.float32, "correction and decay records must remain FP32")
@@ -279,48 +292,52 @@ def _verify(g, beta, q, k, v, checkpoint_state, replay_cache, query_start_loc, s
             and (key_record.dtype == torch.float32 or (qk_already_normalized and key_record.dtype == k.dtype)),
             "low-precision key records require already-normalized input dtype",
         )
-        _require(all(t.stride(-1) == 1 for t in (corr, key_record, decay_record)),
+        rs, key_strides, decay_strides = corr.stride(), key_record.stride(), decay_record.stride()
+        _require(rs[-1] == 1 and key_strides[-1] == 1 and decay_strides[-1] == 1,
                  "typed record innermost dimensions must be contiguous")
-        key_strides = tuple(key_record.stride()[:3])
-        decay_strides = tuple(decay_record.stride())
+        key_strides = key_strides[:3]
     else:
         corr = key_record = decay_record = replay_cache
-        _require(corr.ndim == 4 and tuple(corr.shape[1:]) == (HV, spec_query_len, V + K + 1),
+        rshape = corr.shape
+        _require(len(rshape) == 4 and rshape[1] == HV and rshape[2] == spec_query_len and rshape[3] == V + K + 1,
                  "packed replay record shape is incompatible")
         _require(corr.dtype == torch.float32, "packed records must remain FP32")
-        _require(corr.stride(-1) == 1, "packed record innermost dimension must be contiguous")
-        key_strides = tuple(corr.stride()[:3])
-        decay_strides = tuple(corr.stride()[:3])
-    _require(corr.shape[0] >= 1, "replay buffer has no rows")
-    _require(state_indices.ndim == 1, "state indices must be one-dimensional")
-    _require(query_start_loc.ndim == 1 and query_start_loc.shape[0] == state_indices.shape[0] + 1,
-             "query metadata is incompatible")
-    _require(total <= state_indices.shape[0] * spec_query_len, "speculative decode input exceeds its activation capacity")
-    _require(query_start_loc.dtype in (torch.int32, torch.int64) and state_indices.dtype in (torch.int32, torch.int64),
+        rs = corr.stride()
+        _require(rs[3] == 1, "packed record innermost dimension must be contiguous")
+        key_strides = decay_strides = rs[:3]
+    _require(rshape[0] >= 1, "replay buffer has no rows")
+    sshape, lshape = state_indices.shape, query_start_loc.shape
+    _require(len(sshape) == 1, "state indices must be one-dimensional")
+    _require(len(lshape) == 1 and lshape[0] == sshape[0] + 1, "query metadata is incompatible")
+    batch = sshape[0]
+    _require(total <= batch * spec_query_len, "speculative decode input exceeds its activation capacity")
+    _require(query_start_loc.dtype in _INDEX_DTYPES and state_indices.dtype in _INDEX_DTYPES,
              "query metadata must be int32 or int64")
     dev = q.device
     _require(
-        all(t_.device == dev for t_ in (k, v, g, beta, checkpoint_state, corr, key_record, decay_record,
-                                         query_start_loc, state_indices))
+        k.device == dev and v.device == dev and g.device == dev and beta.device == dev
+        and checkpoint_state.device == dev and corr.device == dev and key_record.device == dev
+        and decay_record.device == dev and query_start_loc.device == dev and state_indices.device == dev
         and (out is None or out.device == dev),
         "inputs must be on the same device",
     )
     if scale is None:
         scale = K**-0.5
     if out is None:
-        out = torch.empty(1, total, HV, V, dtype=v.dtype, device=v.device)
-    _require(tuple(out.shape) == (1, total, HV, V) and out.stride()[2:] == (V, 1) and out.dtype == v.dtype,
+        out = torch.empty(1, total, HV, V, dtype=v.dtype, device=dev)
+    os_ = out.stride()
+    _require(tuple(out.shape) == (1, total, HV, V) and os_[2] == V and os_[3] == 1 and out.dtype == v.dtype,
              "output shape or layout is incompatible")
-    batch = state_indices.shape[0]
     if total == 0 or batch == 0:
         return out
+    cs = checkpoint_state.stride()
     config = [
-        batch, total, H, HV, spec_query_len, nb, corr.shape[0], NULL_BLOCK_ID,
-        q.stride(1), k.stride(1), v.stride(1), g2.stride(0), beta2.stride(0),
-        checkpoint_state.stride(0), checkpoint_state.stride(1), checkpoint_state.stride(2),
-        corr.stride(0), corr.stride(1), corr.stride(2),
+        batch, total, H, HV, spec_query_len, nb, rshape[0], NULL_BLOCK_ID,
+        qs[1], ks[1], vs[1], gs[0], bs[0],
+        cs[0], cs[1], cs[2],
+        rs[0], rs[1], rs[2],
         *key_strides, *decay_strides,
-        out.stride(1), query_start_loc.stride(0), state_indices.stride(0),
+        os_[1], query_start_loc.stride(0), state_indices.stride(0),
     ]
     flags = (0 if soa else _RECORD_PACKED) | (0 if qk_already_normalized else _NORMALIZE_QK)
     if gate is None:
