@@ -65,6 +65,10 @@ struct VerifyTcShape {
   static constexpr int B2_BYTES = 2 * B2_SLAB;
   static constexpr int B_SLAB = NB * 128;
   static constexpr int B_BYTES = 4 * B_SLAB;
+  // Q = 8 (two CTAs per SM leave shared memory to spare): X in fp32, row j at
+  // j * 512 bytes, for the Gram on every warp (gram_all_warps)
+  static constexpr bool GRAM_ALL = QT >= 8;
+  static constexpr int X32_BYTES = GRAM_ALL ? NJ * DIM * 4 : 0;
   struct Window {  // per-unit scalars
     float A[QT];
     float beta[QT];
@@ -80,12 +84,13 @@ struct VerifyTcShape {
     float gpart[4][QT * QT];  // Gram partial sums per K slab
     Window win[2];
   };
-  // tile | pass-2 operand | pass-1 operand | scalars; the dynamic shared memory
-  // base is 1024-byte aligned (checked at run time), as the 128-byte swizzle
-  // atoms require
-  static constexpr int SMEM = TILE + B2_BYTES + B_BYTES + static_cast<int>(sizeof(Small));
+  // tile | pass-2 operand | pass-1 operand | fp32 X (Q = 8) | scalars; the
+  // dynamic shared memory base is 1024-byte aligned (checked at run time), as
+  // the 128-byte swizzle atoms require
+  static constexpr int SMEM = TILE + B2_BYTES + B_BYTES + X32_BYTES + static_cast<int>(sizeof(Small));
   static_assert(NB <= static_cast<int>(D2_COL) && (NB == 16 || NB == 32), "accumulator columns");
   static_assert(NJ <= NB2, "pass-2 operand rows");
+  static_assert(!GRAM_ALL || QT * QT * 4 == kVerifyThreads, "gram_all_warps: four threads per Gram pair");
   static_assert(B_SLAB % 1024 == 0 && B2_SLAB % 1024 == 0, "operand slabs must stay 1024-byte aligned");
 };
 
@@ -147,15 +152,60 @@ __device__ __forceinline__ void gram_partials(const unsigned char *bop, float (*
   }
 }
 
-// gram_finalize: thread `pr` (< Q^2) sums pair pr over the four slabs and
-// scales it by the decay product D[t][s] = prod_{s<r<=t} dec[r]:
+// gram_all_warps (Q = 8: Q^2 = 64 pairs x 4 K quarters = 256 threads): thread
+// 4 pr + sq sums pair pr's products over K elements 32 sq .. 32 sq + 31 from
+// the fp32 copy of X (rows `pair` = a | b << 8, 512 bytes apart), two lane
+// shuffles add the four quarters, and lane sq = 0 stores part[0][pr].  The
+// eight lanes of a quarter-warp start at eight different 16-byte chunks (the
+// chunk order is rotated by 2 sq + pr % 2), so the 128-bit reads are free of
+// bank conflicts.  No reduce-scatter: at Q = 8 the one in gram_partials is
+// ~4x the instructions, all on warps 4-7.
+template <int QT>
+__device__ __forceinline__ void gram_all_warps(const float *x32, float (*part)[QT * QT], int pair, int tid) {
+  const int pr = tid >> 2, sq = tid & 3;
+  const float4 *xa = reinterpret_cast<const float4 *>(x32 + (pair & 0xff) * 128 + sq * 32);
+  const float4 *xb = reinterpret_cast<const float4 *>(x32 + (pair >> 8) * 128 + sq * 32);
+  const int rot = 2 * sq + (pr & 1);
+  float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int cc = (c + rot) & 7;
+    const float4 a = xa[cc], b = xb[cc];
+    acc0 = fmaf(a.x, b.x, acc0);
+    acc1 = fmaf(a.y, b.y, acc1);
+    acc0 = fmaf(a.z, b.z, acc0);
+    acc1 = fmaf(a.w, b.w, acc1);
+  }
+  float acc = acc0 + acc1;
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  if (sq == 0) part[0][pr] = acc;
+}
+
+// The X rows (a, b) of Gram pair pr, packed a | b << 8, in gram_partials'
+// order: k_s . k_t for t = 1..Q-1, s < t, then k_s . q_t for t = 0..Q-1, s <= t.
+template <int QT>
+__device__ __forceinline__ int gram_pair_rows(int pr) {
+  constexpr int NKK = QT * (QT - 1) / 2;
+  const int kind = pr >= NKK ? 1 : 0;
+  int rem = kind ? pr - NKK : pr, t = kind ? 0 : 1;
+  while (rem >= (kind ? t + 1 : t)) {
+    rem -= kind ? t + 1 : t;
+    ++t;
+  }
+  return rem | ((kind ? QT + t : t) << 8);
+}
+
+// gram_finalize: thread `pr` (< Q^2) sums pair pr over the four slabs (or
+// takes the whole sum from slab 0, SUMMED) and scales it by the decay product
+// D[t][s] = prod_{s<r<=t} dec[r]:
 //     mkk[t][s] = D[t][s] (k_s . k_t)  for s < t,
 //     mkq[t][s] = D[t][s] (k_s . q_t)  for s <= t.
-template <int QT>
+template <int QT, bool SUMMED>
 __device__ __forceinline__ void gram_finalize(const float (*part)[QT * QT], const float *dec, float (*mkk)[QT],
                                               float (*mkq)[QT], int pr) {
   constexpr int NKK = QT * (QT - 1) / 2;
-  const float sum = (part[0][pr] + part[1][pr]) + (part[2][pr] + part[3][pr]);
+  const float sum = SUMMED ? part[0][pr] : (part[0][pr] + part[1][pr]) + (part[2][pr] + part[3][pr]);
   const int kind = pr >= NKK ? 1 : 0;
   int rem = kind ? pr - NKK : pr, t = kind ? 0 : 1;
   while (rem >= (kind ? t + 1 : t)) {
@@ -225,7 +275,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   unsigned char *tile = smem_raw;
   unsigned char *b2op = smem_raw + Sh::TILE;  // pass-2 operand: bf16(X)
   unsigned char *bop = b2op + Sh::B2_BYTES;    // pass-1 operand: [hi(X); lo(X)]
-  Small &sm = *reinterpret_cast<Small *>(bop + Sh::B_BYTES);
+  float *x32 = reinterpret_cast<float *>(bop + Sh::B_BYTES);  // fp32 X (Q = 8)
+  Small &sm = *reinterpret_cast<Small *>(bop + Sh::B_BYTES + Sh::X32_BYTES);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -349,6 +400,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     ptx::tmem_alloc(&sm.tmem, Sh::TMEM_COLS);
     ptx::tmem_relinquish();
   }
+  const int gpair = Sh::GRAM_ALL ? gram_pair_rows<QT>(tid >> 2) : 0;  // this thread's Gram pair (Q = 8)
   Inputs ic;
   load_inputs(ic, c0, m0);
   ptx::tc_fence_before_sync();
@@ -448,6 +500,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
 #pragma unroll
           for (int e = 0; e < EPL; ++e) x[e] *= p.scale;
         }
+        if constexpr (Sh::GRAM_ALL)
+          *reinterpret_cast<float4 *>(x32 + j * DIM + lane * EPL) = make_float4(x[0], x[1], x[2], x[3]);
         float hi[EPL], lo[EPL];
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
@@ -530,7 +584,11 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         }
       }
       // ---- ... the Gram partial sums and the next units' loads ---------------- //
-      if (warp >= 4) gram_partials<QT, NJ, Sh::B_SLAB>(bop, sm.gpart, warp - 4, lane);
+      if constexpr (Sh::GRAM_ALL) {
+        gram_all_warps<QT>(x32, sm.gpart, gpair, tid);
+      } else {
+        if (warp >= 4) gram_partials<QT, NJ, Sh::B_SLAB>(bop, sm.gpart, warp - 4, lane);
+      }
       prefetch();
       ptx::fence_proxy_async_smem();  // pass-2 operand -> tensor-core reads
       ptx::tc_fence_before_sync();
@@ -550,7 +608,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         ptx::mma_commit(&sm.mma_bar);
       }
       // ---- Gram coefficients and decay products (off warp 0, which issues) ---- //
-      if (tid >= 128 && tid < 128 + QT * QT) gram_finalize<QT>(sm.gpart, w.dec, w.mkk, w.mkq, tid - 128);
+      if (tid >= 128 && tid < 128 + QT * QT) gram_finalize<QT, Sh::GRAM_ALL>(sm.gpart, w.dec, w.mkk, w.mkq, tid - 128);
       if (tid == 224) {
         float a = 1.f;
 #pragma unroll
