@@ -32,6 +32,8 @@ CASES = [
     (5, torch.bfloat16, "packed", True, 2, 4, torch.float32),
     (8, torch.bfloat16, "soa", False, 2, 4, torch.float32),
     (8, torch.float32, "packed", False, 4, 4, torch.float32),
+    (7, torch.float16, "packed", True, 2, 4, torch.float32),
+    (6, torch.bfloat16, "soa", True, 1, 4, torch.float32),
     (4, torch.bfloat16, "packed", False, 2, 4, torch.bfloat16),
 ]
 
