@@ -44,6 +44,29 @@ def _cuda_home() -> Path:
     raise RuntimeError("GDN RecoverSSM build: nvcc not found (set CUDA_HOME)")
 
 
+def _host_cxx() -> str:
+    """The C++ compiler of the torch-op library: ``GDN_RSSM_CXX``, else the
+    ``g++`` on PATH.  The library must link the SHARED C++ runtime that torch
+    itself uses: a private static copy (what a toolchain whose shared
+    libstdc++ link is missing produces) gives the library its own iostreams
+    and exception runtime, and formatting a TORCH_CHECK message there crashes
+    the process.  ``_check_shared_runtime`` refuses such a build."""
+    return os.environ.get("GDN_RSSM_CXX") or shutil.which("g++") or os.environ.get("CXX", "g++")
+
+
+def _check_shared_runtime(lib: Path) -> None:
+    nm = shutil.which("nm")
+    if nm is None:
+        return
+    out = subprocess.run([nm, "-D", "--defined-only", str(lib)], capture_output=True, text=True).stdout
+    if "__cxa_throw" in out or "_ZNSt8ios_base4InitC" in out:
+        lib.unlink()
+        raise RuntimeError(
+            f"GDN RecoverSSM build: {lib.name} embeds a static C++ runtime (its compiler linked libstdc++.a); "
+            "build it with a g++ that links the shared libstdc++ (set GDN_RSSM_CXX)"
+        )
+
+
 def _headers():
     return list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
 
@@ -94,6 +117,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         objs = list(pool.map(compile_one, CUDA_SOURCES))
     if force or _stale(CAPI_LIB, objs):
         _run([nvcc, *ARCH, "-shared", "-o", str(CAPI_LIB), *map(str, objs)])
+        _check_shared_runtime(CAPI_LIB)
         if verbose:
             print("linked", CAPI_LIB.name, flush=True)
 
@@ -106,7 +130,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         incs = [f"-I{p}" for p in cpp_extension.include_paths()] + [f"-I{cuda / 'include'}", f"-I{INCLUDE}"]
         libdirs = cpp_extension.library_paths()
         cmd = [
-            os.environ.get("CXX", "g++"),
+            _host_cxx(),
             "-O2",
             "-std=c++17",
             "-fPIC",
@@ -127,6 +151,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
             *[f"-Wl,-rpath,{d}" for d in libdirs],
         ]
         _run(cmd)
+        _check_shared_runtime(TORCH_LIB)
         if verbose:
             print("linked", TORCH_LIB.name, flush=True)
     return {"capi": CAPI_LIB, "torch": TORCH_LIB}

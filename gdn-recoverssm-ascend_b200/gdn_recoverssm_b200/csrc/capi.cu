@@ -158,7 +158,8 @@ static int verify_impl(const void *q, const void *k, const void *v, const void *
 
   const bool packed = (flags & GDN_RSSM_RECORD_PACKED) != 0;
   const bool normalize = (flags & GDN_RSSM_NORMALIZE_QK) != 0;
-  GDN_REQUIRE((flags & ~(GDN_RSSM_RECORD_PACKED | GDN_RSSM_NORMALIZE_QK | GDN_RSSM_VERIFY_TEST_NO_TILE)) == 0,
+  GDN_REQUIRE((flags & ~(GDN_RSSM_RECORD_PACKED | GDN_RSSM_NORMALIZE_QK | GDN_RSSM_VERIFY_TEST_NO_TILE |
+                          GDN_RSSM_VERIFY_CUDA_CORES)) == 0,
               "unknown verify flags");
   GDN_REQUIRE(p.null_block == 0, "the null block id must be 0 (page zero is reserved)");
   GDN_REQUIRE(key_dim == value_dim && (key_dim == 32 || key_dim == 64 || key_dim == 128),
@@ -347,6 +348,9 @@ int gdn_rssm_commit_plan(gdn_rssm_index_view num_accepted, gdn_rssm_index_view r
                 "block table must be two-dimensional with a positive width");
     GDN_REQUIRE(view_ok(num_computed), "align mode needs num_computed_tokens");
     GDN_REQUIRE(block_size >= spec_query_len, "align block size must cover one speculative window");
+    // the per-context plan does its align arithmetic in 32 bits, as the reference does
+    GDN_REQUIRE(block_size < (int64_t{1} << 31) && block_table.cols < (int64_t{1} << 31),
+                "align block size and block table width must stay below 2^31");
   }
   CommitPlanParams p{};
   p.accepted = num_accepted;

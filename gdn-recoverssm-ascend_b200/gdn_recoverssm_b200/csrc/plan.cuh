@@ -28,6 +28,17 @@ constexpr int kConvChannelsPerCta = 1024;  // largest chunk
 constexpr int kConvSmemLimit = 48 * 1024;  // staging of the contiguous path: 3 chunks
 
 
+// 32-bit two's-complement arithmetic of the per-context plan: the reference
+// kernel loads the accepted and computed counts as int32 and does the align
+// arithmetic in int32 (kernels.py:978-1035), so sums past 2^31 wrap there and
+// must wrap here too.  Done on uint32 to keep the wrap defined in C++.
+__device__ __forceinline__ int32_t add_wrap32(int32_t a, int32_t b) {
+  return static_cast<int32_t>(static_cast<uint32_t>(a) + static_cast<uint32_t>(b));
+}
+__device__ __forceinline__ int32_t mul_wrap32(int32_t a, int32_t b) {
+  return static_cast<int32_t>(static_cast<uint32_t>(a) * static_cast<uint32_t>(b));
+}
+
 __global__ void commit_plan_kernel(const CommitPlanParams p) {
   // launched as a programmatic dependent of the kernel before it (the sampler
   // in serving, verify in a bench step): wait for it before reading its
@@ -40,26 +51,29 @@ __global__ void commit_plan_kernel(const CommitPlanParams p) {
   const int64_t source = load_index(p.state, r);
   const int64_t req = p.request.data ? load_index(p.request, r) : r;
   bool row_ok = true;
-  const int64_t acc = load_index_checked(p.accepted, req, row_ok);
+  const int32_t acc = static_cast<int32_t>(load_index_checked(p.accepted, req, row_ok));
   const int64_t bos = load_index(p.qsl, r), eos = load_index(p.qsl, r + 1);
   const int32_t qlen = static_cast<int32_t>(eos - bos);
-  int64_t n = acc > 0 ? acc : 0;
+  int32_t n = acc > 0 ? acc : 0;
   n = n < qlen ? n : qlen;
-  n = n < p.Q ? n : p.Q;
-  int64_t fin = source, boundary = nul, blen = 0, colv = 0, c = 0;
+  n = n < p.Q ? n : static_cast<int32_t>(p.Q);
+  int64_t fin = source, boundary = nul;
+  int32_t blen = 0, colv = 0, c = 0;
   const bool align = p.table.data != nullptr;
   if (align) {
     c = static_cast<int32_t>(load_index_checked(p.computed, req, row_ok));
     if (req < 0 || req >= p.table.rows) row_ok = false;
-    const int64_t W = p.table.cols, B = p.block_size;
-    const int64_t end = c + n;
-    colv = floordiv(end - 1 > 0 ? end - 1 : 0, B);
+    const int32_t W = static_cast<int32_t>(p.table.cols), B = static_cast<int32_t>(p.block_size);  // B >= 1
+    const int32_t end = add_wrap32(c, n);
+    const int32_t last = add_wrap32(end, -1);
+    colv = (last > 0 ? last : 0) / B;
     colv = colv < W - 1 ? colv : W - 1;
     fin = row_ok ? load_table(p.table, req, colv) : nul;
-    const int64_t nxt = (floordiv(c, B) + 1) * B;
+    // c >= 0 on every row whose outputs are kept, where / is floor division
+    const int32_t nxt = mul_wrap32(add_wrap32(c / B, 1), B);
     const bool crosses = end >= nxt;
-    blen = nxt - c;
-    const int64_t bcol = floordiv(nxt, B) - 1;
+    blen = add_wrap32(nxt, -c);
+    const int32_t bcol = nxt / B - 1;
     boundary = (row_ok && crosses && bcol >= 0 && bcol < W) ? load_table(p.table, req, bcol) : nul;
   }
   const bool geometry = bos >= 0 && bos <= eos && qlen <= p.Q;
@@ -69,12 +83,12 @@ __global__ void commit_plan_kernel(const CommitPlanParams p) {
     valid = valid && c >= 0;
     if (!(boundary > nul && boundary < p.num_blocks)) blen = 0;
   }
-  p.lens[r] = valid ? static_cast<int32_t>(n) : 0;
+  p.lens[r] = valid ? n : 0;
   p.finals[r] = static_cast<int32_t>(valid ? fin : nul);
   p.boundaries[r] = static_cast<int32_t>(valid ? boundary : nul);
-  p.boundary_lens[r] = valid ? static_cast<int32_t>(blen) : 0;
+  p.boundary_lens[r] = valid ? blen : 0;
   p.valid[r] = valid ? 1 : 0;
-  p.col[r] = static_cast<int32_t>(colv);
+  p.col[r] = colv;
 }
 
 

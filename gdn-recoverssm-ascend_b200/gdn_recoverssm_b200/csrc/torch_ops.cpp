@@ -226,6 +226,13 @@ void fold_ext(const Tensor &state, const Tensor &correction, const Tensor &key, 
   TORCH_CHECK(correction.scalar_type() == at::kFloat && correction.dim() == 4 && correction.stride(3) == 1 &&
                   config[11] == correction.stride(1) && config[12] == correction.stride(2),
               "GDN RecoverSSM: fold config does not match the correction records");
+  // the kernel bounds pages by config[5] and record rows by config[6]: both
+  // must lie inside the tensors this op was given (the address tables of the
+  // other layers are trusted to describe pools and records at least as large)
+  TORCH_CHECK(config[5] > 0 && config[5] <= state.size(0),
+              "GDN RecoverSSM: fold page bound exceeds the state pool (", config[5], " > ", state.size(0), ")");
+  TORCH_CHECK(config[6] > 0 && config[6] <= correction.size(0) && config[0] <= config[7],
+              "GDN RecoverSSM: fold record rows exceed the correction records or rows exceed the plan capacity");
   const int64_t V = state.size(2), K = state.size(3);
   if (packed) {
     TORCH_CHECK(correction.size(3) == V + K + 1, "GDN RecoverSSM: packed record width must be V + K + 1");
@@ -234,6 +241,8 @@ void fold_ext(const Tensor &state, const Tensor &correction, const Tensor &key, 
                     decay.stride(2) == 1 && config[13] == key.stride(1) && config[14] == key.stride(2) &&
                     config[15] == decay.stride(1) && config[16] == decay.stride(2) && key.size(1) == config[3],
                 "GDN RecoverSSM: fold config does not match the typed records");
+    TORCH_CHECK(config[6] <= key.size(0) && config[6] <= decay.size(0),
+                "GDN RecoverSSM: fold record rows exceed the key / decay records");
   }
   auto src = index_view(source, state, "source");
   const c10::cuda::CUDAGuard guard(state.device());

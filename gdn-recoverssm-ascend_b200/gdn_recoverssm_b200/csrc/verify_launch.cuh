@@ -38,21 +38,21 @@ constexpr bool verify_uses_tensor_cores() {
   return GDN_RSSM_VERIFY_TENSOR_CORES && DIM == 128 && std::is_same<St, float>::value;
 }
 
-template <int DIM, int QT, typename Act, typename St>
-int launch_verify_variant(VerifyLaunch &L) {
-  constexpr bool tc = verify_uses_tensor_cores<DIM, St>();
+// TC: the tensor-core kernel (verify_tc.cuh), else the CUDA-core kernel.
+template <int DIM, int QT, typename Act, typename St, bool TC>
+int launch_verify_kernel(VerifyLaunch &L) {
   // tensor-core kernel: whole-height boxes (4 copies per tile); CUDA-core
   // kernel: 32-row quarters, each on its own mbarrier
   CUtensorMap map;
-  int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, tc ? DIM : 32, L.p.value_heads, L.p.blocks,
+  int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, TC ? DIM : 32, L.p.value_heads, L.p.blocks,
                             L.state_bs, L.state_hs, L.state_vs);
   if (rc != GDN_RSSM_OK) return rc;
-  constexpr int smem = tc ? verify_tc_smem_bytes<QT, Act>() : verify_smem_bytes<DIM, QT, Act, St>();
+  constexpr int smem = TC ? verify_tc_smem_bytes<QT, Act>() : verify_smem_bytes<DIM, QT, Act, St>();
   // the tensor-core kernel has a separate instantiation for the fused gating
   // prologue, so the plain form keeps its register budget
   const int gated = (L.p.flags & kGateInKernel) ? 1 : 0;
   void (*kernel)(const CUtensorMap, const VerifyParams) = nullptr;
-  if constexpr (tc) {
+  if constexpr (TC) {
     kernel = gated ? verify_tc_kernel<QT, Act, true> : verify_tc_kernel<QT, Act, false>;
   } else {
     kernel = verify_kernel<DIM, QT, Act, St>;
@@ -71,7 +71,7 @@ int launch_verify_variant(VerifyLaunch &L) {
   const int64_t units = L.p.rows * L.p.value_heads;
   if (units <= 0) return GDN_RSSM_OK;
   int64_t grid = units;  // CUDA-core kernel: one CTA per (row, value head) unit
-  if constexpr (tc) {
+  if constexpr (TC) {
     // tensor-core kernel: as many CTAs as fit at once, each walking units
     // blockIdx.x + k * gridDim.x
     grid = std::min<int64_t>(units, static_cast<int64_t>(sm_count_current_device()) * verify_tc_min_blocks<QT>());
@@ -79,6 +79,16 @@ int launch_verify_variant(VerifyLaunch &L) {
   kernel<<<static_cast<unsigned>(grid), kVerifyThreads, smem, L.stream>>>(map, L.p);
   GDN_CUDA(cudaGetLastError());
   return GDN_RSSM_OK;
+}
+
+template <int DIM, int QT, typename Act, typename St>
+int launch_verify_variant(VerifyLaunch &L) {
+  if constexpr (verify_uses_tensor_cores<DIM, St>()) {
+    if (L.p.flags & GDN_RSSM_VERIFY_CUDA_CORES) return launch_verify_kernel<DIM, QT, Act, St, false>(L);
+    return launch_verify_kernel<DIM, QT, Act, St, true>(L);
+  } else {
+    return launch_verify_kernel<DIM, QT, Act, St, false>(L);
+  }
 }
 
 template <int DIM, typename Act, typename St>

@@ -79,7 +79,10 @@ struct VerifyTcShape {
   struct Small {
     uint64_t tile_bar;
     uint64_t mma_bar;
-    uint64_t meta_raw[3];  // bos, eos, slot of the unit two ahead, as copied (cp.async)
+    // bos, eos, slot of the unit two ahead, as copied (cp.async), by the
+    // parity of the walk step that copied them: a warp still decoding step
+    // i's copy never races the copy step i + 1 starts before any barrier
+    uint64_t meta_raw[2][3];
     uint32_t tmem;
     float gpart[4][QT * QT];  // Gram partial sums per K slab
     Window win[2];
@@ -94,16 +97,22 @@ struct VerifyTcShape {
   static_assert(B_SLAB % 1024 == 0 && B2_SLAB % 1024 == 0, "operand slabs must stay 1024-byte aligned");
 };
 
-template <int QT, typename Act>
-constexpr int verify_tc_smem_bytes() {
-  return VerifyTcShape<QT, Act>::SMEM;
-}
-
 // Resident CTAs per SM: three up to Q = 4 (74 KB of shared memory each), two
 // at Q = 8.
 template <int QT>
 constexpr int verify_tc_min_blocks() {
   return QT >= 8 ? 2 : 3;
+}
+
+// Shared memory of one SM (228 KB) and what the runtime reserves per CTA.
+constexpr int kSmemPerSm = 233472;
+constexpr int kSmemReservedPerCta = 1024;
+
+template <int QT, typename Act>
+constexpr int verify_tc_smem_bytes() {
+  static_assert(verify_tc_min_blocks<QT>() * (VerifyTcShape<QT, Act>::SMEM + kSmemReservedPerCta) <= kSmemPerSm,
+                "the verify CTAs of one SM must fit its shared memory");
+  return VerifyTcShape<QT, Act>::SMEM;
 }
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
@@ -302,23 +311,22 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   // qsl / slot entries into shared memory (no registers held, no stall);
   // everyone decodes them after the next CTA barrier.
   constexpr int kMetaThread = 64;
-  auto load_meta_async = [&](const TcCursor &c, bool in_range) {  // thread kMetaThread
+  auto load_meta_async = [&](uint64_t *raw, const TcCursor &c, bool in_range) {  // thread kMetaThread
     if (!in_range) {
-      sm.meta_raw[0] = 0;
-      sm.meta_raw[1] = 0;
-      sm.meta_raw[2] = ~0ull;  // decodes to slot -1 for either index dtype
+      raw[0] = 0;
+      raw[1] = 0;
+      raw[2] = ~0ull;  // decodes to slot -1 for either index dtype
       return;
     }
     const int qb = p.qsl_dtype == GDN_RSSM_I64 ? 8 : 4, ib = p.index_dtype == GDN_RSSM_I64 ? 8 : 4;
     const char *qsl = static_cast<const char *>(p.qsl);
     const char *idx = static_cast<const char *>(p.indices);
-    ptx::cp_async_small(&sm.meta_raw[0], qsl + static_cast<int64_t>(c.row) * p.qsl_stride * qb, qb);
-    ptx::cp_async_small(&sm.meta_raw[1], qsl + static_cast<int64_t>(c.row + 1) * p.qsl_stride * qb, qb);
-    ptx::cp_async_small(&sm.meta_raw[2], idx + static_cast<int64_t>(c.row) * p.index_stride * ib, ib);
+    ptx::cp_async_small(&raw[0], qsl + static_cast<int64_t>(c.row) * p.qsl_stride * qb, qb);
+    ptx::cp_async_small(&raw[1], qsl + static_cast<int64_t>(c.row + 1) * p.qsl_stride * qb, qb);
+    ptx::cp_async_small(&raw[2], idx + static_cast<int64_t>(c.row) * p.index_stride * ib, ib);
     ptx::cp_async_commit();
   };
-  auto decode_meta = [&]() {
-    const uint64_t *raw = sm.meta_raw;
+  auto decode_meta = [&](const uint64_t *raw) {
     auto val = [](uint64_t b, int32_t dt) {
       return dt == GDN_RSSM_I64 ? static_cast<int64_t>(b)
                                 : static_cast<int64_t>(static_cast<int32_t>(static_cast<uint32_t>(b)));
@@ -415,7 +423,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   for (int64_t u = blockIdx.x, i = 0; u < units && ok; u += G, ++i) {
     Inputs in;  // one unit ahead
     auto prefetch = [&]() {
-      if (tid == kMetaThread) load_meta_async(c2, u + 2 * G < units);  // two units ahead
+      if (tid == kMetaThread) load_meta_async(sm.meta_raw[i & 1], c2, u + 2 * G < units);  // two units ahead
       load_inputs(in, c1, m1);
     };
     const int64_t row = c0.row;
@@ -657,7 +665,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     }
     ic = in;
     m0 = m1;
-    m1 = decode_meta();  // copied before the last CTA barrier
+    m1 = decode_meta(sm.meta_raw[i & 1]);  // copied before the last CTA barrier
     c0 = c1;
     c1 = c2;
     c2.advance(dq, dr, HV32);

@@ -5,8 +5,11 @@ Distributions: checkpoint states ~ N(0, 0.1^2); q, k ~ N(0, 1) then
 L2-normalised per head; v ~ N(0, 1); g = -softplus(N(0, 1)) (so the decay
 exp(g) lies in (0, 1)); beta = sigmoid(N(0, 1)).  Metadata (slots, accepted
 lengths, block tables, positions) comes from a CPU generator so that every
-rank of a sharded run sees identical metadata; the large tensors come from a
-device generator seeded per (config, rank).
+rank of a sharded run sees identical metadata.  Every per-head tensor (q, k
+per key head; v, g, beta, the state tiles and the raw gate inputs per value
+head) comes from a device generator seeded by (seed, config, tensor, global
+head index) and drawn in fixed-size pieces, so a rank's shard holds exactly
+the values of its heads in the unsharded workload.
 
 Configurations (``CONFIGS``):
   0  B=4,    H=HV=4,      K=V=64,  Q=4, fp32 everything, pool 8, none mode
@@ -156,13 +159,23 @@ def metadata(cfg: int, seed: int = 0, rows: int | None = None, pool: int | None 
     return meta
 
 
+_STATE_PAGES_PER_DRAW = 256  # state pages drawn per generator call (fixed: values do not depend on the pool size)
+
+
+def _head_generator(dev, seed: int, cfg: int, kind: int, head: int):
+    """The generator of one (tensor, global head): independent of world size
+    and rank."""
+    return torch.Generator(device=dev).manual_seed(
+        (seed + 1) * 1_000_003 + cfg * 100_003 + kind * 10_007 + head * 101 + 17)
+
+
 def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv_dim: int = 0,
          rows: int | None = None, pool: int | None = None, gated: bool = False) -> Workload:
     """Allocate and fill one configuration's tensors on ``device`` (this
-    rank's head shard).  ``gated`` adds the raw gate inputs of the
-    fused-gating verify: a, b ~ N(0, 1) in the activation dtype, A_log =
-    log(U(1, 16)) and dt_bias = softplus^-1(dt) with dt log-uniform in
-    [1e-3, 1e-1] per value head."""
+    rank's head shard: exactly those heads' values of the unsharded
+    workload).  ``gated`` adds the raw gate inputs of the fused-gating verify:
+    a, b ~ N(0, 1) in the activation dtype, A_log = log(U(1, 16)) and dt_bias
+    = softplus^-1(dt) with dt log-uniform in [1e-3, 1e-1] per value head."""
     spec = spec_of(cfg, rows, pool)
     B, H, HV, D, Q, pool = spec["B"], spec["H"], spec["HV"], spec["D"], spec["Q"], spec["pool"]
     shard = head_shard(H, HV, world, rank)
@@ -170,19 +183,32 @@ def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv
     act = spec["act"]
     meta = metadata(cfg, seed, rows, pool)
     dev = torch.device(device)
-    gen = torch.Generator(device=dev).manual_seed(7919 * (seed + 1) + 104729 * rank + cfg)
     T = B * Q
-    q = _unit_norm(torch.randn(1, T, H, D, generator=gen, device=dev)).to(act)
-    k = _unit_norm(torch.randn(1, T, H, D, generator=gen, device=dev)).to(act)
-    v = torch.randn(1, T, HV, D, generator=gen, device=dev).to(act)
-    g = -torch.nn.functional.softplus(torch.randn(T, HV, generator=gen, device=dev))
-    beta = torch.sigmoid(torch.randn(T, HV, generator=gen, device=dev))
+
+    def key_head(kind, j, shape):  # local key head j
+        return torch.randn(shape, generator=_head_generator(dev, seed, cfg, kind, shard.key_begin + j), device=dev)
+
+    def value_head(kind, j, shape):  # local value head j
+        return torch.randn(shape, generator=_head_generator(dev, seed, cfg, kind, shard.value_begin + j), device=dev)
+
+    q = torch.empty(1, T, H, D, dtype=act, device=dev)
+    k = torch.empty(1, T, H, D, dtype=act, device=dev)
+    for j in range(H):
+        q[0, :, j] = _unit_norm(key_head(0, j, (T, D))).to(act)
+        k[0, :, j] = _unit_norm(key_head(1, j, (T, D))).to(act)
+    v = torch.empty(1, T, HV, D, dtype=act, device=dev)
+    g = torch.empty(T, HV, device=dev)
+    beta = torch.empty(T, HV, device=dev)
     state = torch.empty(pool, HV, D, D, device=dev)
-    # fill page by page to keep the temporary small on large pools
-    chunk = max(1, (1 << 28) // (HV * D * D))
-    for p0 in range(0, pool, chunk):
-        p1 = min(pool, p0 + chunk)
-        state[p0:p1].normal_(0.0, 0.1, generator=gen)
+    for j in range(HV):
+        v[0, :, j] = value_head(2, j, (T, D)).to(act)
+        gb = value_head(3, j, (2, T))
+        g[:, j] = -torch.nn.functional.softplus(gb[0])
+        beta[:, j] = torch.sigmoid(gb[1])
+        gen = _head_generator(dev, seed, cfg, 4, shard.value_begin + j)
+        for p0 in range(0, pool, _STATE_PAGES_PER_DRAW):
+            p1 = min(pool, p0 + _STATE_PAGES_PER_DRAW)
+            state[p0:p1, j] = torch.randn((p1 - p0, D, D), generator=gen, device=dev) * 0.1
     records = torch.zeros(B, HV, Q, 2 * D + 1, device=dev)
     out = torch.zeros(1, T, HV, D, dtype=act, device=dev)
     wl = Workload(
@@ -194,15 +220,25 @@ def make(cfg: int, device, *, seed: int = 0, world: int = 1, rank: int = 0, conv
         wl.block_table = meta["block_table"].to(dev)
         wl.num_computed = meta["num_computed"].to(dev)
         wl.block_size = meta["block_size"]
-    if conv_dim:
+    if conv_dim:  # the conv state of this rank's channels (not a head slice of anything)
+        gen = torch.Generator(device=dev).manual_seed(7919 * (seed + 1) + 104729 * rank + cfg)
         wl.conv = torch.randn(pool, conv_dim, 3 + Q - 1, generator=gen, device=dev).to(act)
     if gated:
-        wl.a = torch.randn(T, HV, generator=gen, device=dev).to(act)
-        wl.b = torch.randn(T, HV, generator=gen, device=dev).to(act)
-        wl.A_log = torch.log(torch.rand(HV, generator=gen, device=dev) * 15.0 + 1.0)
-        dt = torch.exp(torch.rand(HV, generator=gen, device=dev) * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
-        wl.dt_bias = dt + torch.log(-torch.expm1(-dt))
+        wl.a = torch.empty(T, HV, dtype=act, device=dev)
+        wl.b = torch.empty(T, HV, dtype=act, device=dev)
+        wl.A_log = torch.empty(HV, device=dev)
+        wl.dt_bias = torch.empty(HV, device=dev)
+        lo, hi = math.log(1e-3), math.log(1e-1)
+        for j in range(HV):
+            ab = value_head(5, j, (2, T))
+            wl.a[:, j] = ab[0].to(act)
+            wl.b[:, j] = ab[1].to(act)
+            u = torch.rand(2, generator=_head_generator(dev, seed, cfg, 6, shard.value_begin + j), device=dev)
+            wl.A_log[j] = torch.log(u[0] * 15.0 + 1.0)
+            dt = torch.exp(u[1] * (hi - lo) + lo)
+            wl.dt_bias[j] = dt + torch.log(-torch.expm1(-dt))
     wl.extra["meta"] = meta
+    wl.extra["shard"] = shard
     return wl
 
 

@@ -82,6 +82,10 @@ enum {
  * gdn_rssm_device_status() reads, releases its tensor memory and exits, and
  * the context stays usable.  Ignored by the other kernels. */
 #define GDN_RSSM_VERIFY_TEST_NO_TILE 0x10000u
+/* Accuracy comparisons: run the CUDA-core verify kernel (fp32 FMAs over the
+ * whole state tile) where the tensor-core kernel would run (K = V = 128, fp32
+ * pool).  Same results within fp32 rounding, slower. */
+#define GDN_RSSM_VERIFY_CUDA_CORES 0x20000u
 
 /* gdn_rssm_fold flags. */
 #define GDN_RSSM_FOLD_PACKED 1u /* records are packed fp32 [R,HV,Q,V+K+1] */
@@ -198,7 +202,13 @@ GDN_RSSM_API int gdn_rssm_verify_gated(const void *q, const void *k, const void 
  * Head/v/token strides come from the config and are shared by all layers.
  * Plan arrays (int32, plan_len entries): plan row = layer_groups[l] *
  * plan_capacity + row; `source` may be any index view (the per-context
- * commit passes the raw state indices).  Only `state` pages are written. */
+ * commit passes the raw state indices).  Only `state` pages are written.
+ * The kernel bounds every page index by config field `blocks` and every
+ * record row by `record_rows`; the library cannot see the sizes behind the
+ * address tables, so the caller guarantees that each layer's pool holds the
+ * pages its plan rows name (at least `blocks` pages, or, in a grouped
+ * commit, its own group's pool size, which the grouped plan enforces) and
+ * that each layer's records hold `record_rows` rows. */
 GDN_RSSM_API int gdn_rssm_fold(const int64_t *state_addrs, const int64_t *state_block_strides,
                   const int64_t *corr_addrs, const int64_t *corr_block_strides,
                   const int64_t *key_addrs, const int64_t *key_block_strides,

@@ -228,6 +228,12 @@ def verify_batch(
     return out, records
 
 
+def _i32(x):
+    """Two's-complement int32 value of an integer (the wrap of the reference
+    kernels' ``.to(tl.int32)`` loads and int32 sums)."""
+    return (int(x) + (1 << 31)) % (1 << 32) - (1 << 31)
+
+
 def _load(arr, i, default=None):
     """Bounded table read; the CUDA kernels treat an out-of-range index as an
     invalid row (the reference would read out of bounds)."""
@@ -254,6 +260,10 @@ def prepare_commit_plan(
     boundary_lens, valid, col``.  Differences from the grouped plan that this
     restatement keeps: an invalid boundary page of a VALID row is stored as is
     (only its length is zeroed, :1059-1066), and ``col`` is stored unmasked.
+    The accepted and computed counts are loaded as int32 and the align
+    arithmetic runs in int32 (:978-1035), so values past 2^31 wrap; the
+    divisions only matter on rows with ``computed >= 0`` (the others are
+    invalid), where floor and truncating division agree.
     """
     Q = int(spec_query_len)
     src = np.asarray(state_indices, dtype=np.int64)
@@ -265,8 +275,9 @@ def prepare_commit_plan(
     for r in range(B):
         req = r if request_indices is None else int(request_indices[r])
         a = _load(acc, req)
+        a = None if a is None else _i32(a)
         bos, eos = int(qsl[r]), int(qsl[r + 1])
-        qlen = eos - bos
+        qlen = _i32(eos - bos)
         source = int(src[r])
         n = min(max(a if a is not None else 0, 0), qlen, Q)
         final, boundary, blen, col = source, NULL_BLOCK_ID, 0, 0
@@ -275,13 +286,14 @@ def prepare_commit_plan(
             c = _load(num_computed, req)
             if c is None or not (0 <= req < block_table.shape[0]):
                 row_ok, c = False, 0
+            c = _i32(c)
             W = block_table.shape[1]
-            end = c + n
-            col = min(max(end - 1, 0) // block_size, W - 1)
+            end = _i32(c + n)
+            col = min(max(_i32(end - 1), 0) // block_size, W - 1)
             final = int(block_table[req, col]) if row_ok else NULL_BLOCK_ID
-            nxt = (c // block_size + 1) * block_size
+            nxt = _i32((c // block_size + 1) * block_size)
             crosses = end >= nxt
-            blen = nxt - c
+            blen = _i32(nxt - c)
             bcol = nxt // block_size - 1
             boundary = int(block_table[req, bcol]) if (row_ok and crosses and 0 <= bcol < W) else NULL_BLOCK_ID
         geometry = bos >= 0 and bos <= eos and qlen <= Q
@@ -347,6 +359,7 @@ def grouped_plan(
             bos, eos = int(qsl[row]), int(qsl[row + 1])
             qlen = eos - bos
             a = _load(samp, req)
+            a = None if a is None else _i32(a)  # loaded .to(tl.int32) (:152)
             row_ok = a is not None
             n = min(max(a if a is not None else 0, 0), qlen, Q)
             final, boundary, blen, col = source, NULL_BLOCK_ID, 0, 0

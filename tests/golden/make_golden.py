@@ -304,6 +304,43 @@ def context_commit_case(K, name, *, align, soa, layers=1, seed=1, D=32, H=2, HV=
     _save(name, **arrays)
 
 
+def plan_int32_case(K, name, *, seed=9, D=32, H=2, HV=4, Q=4):
+    """Per-context align commit whose counts exercise the plan's int32
+    arithmetic: int64 accepted counts past 2^31 (truncated on load), a
+    computed count near 2^31 whose end position and next boundary wrap, an
+    int64 computed count that truncates to a small one, and negative counts."""
+    gen = torch.Generator().manual_seed(seed)
+    blocks, rows, hist, cdim, bs, W = 24, 7, 3, 16, 64, 3
+    states = [torch.randn(blocks, HV, D, D, generator=gen) * 0.1]
+    convs = [torch.randn(blocks, cdim, hist + Q - 1, generator=gen)]
+    r = torch.randn(rows, HV, Q, 2 * D + 1, generator=gen) * 0.1
+    r[..., D : 2 * D] = _unit(torch.randn(rows, HV, Q, D, generator=gen))
+    r[..., 2 * D] = torch.rand(rows, HV, Q, generator=gen) * 0.5 + 0.45
+    records = [r]
+    states0 = [s.clone() for s in states]
+    convs0 = [c.clone() for c in convs]
+    ctx = K.GDNRecoverSSMCommitContext.from_tensors(convs, states, records, spec_query_len=Q, max_num_reqs=rows)
+    big = 1 << 31
+    acc = torch.tensor([big + 3, (1 << 32) + 2, 3, 4, 2, -1, 4], dtype=torch.int64)
+    computed = torch.tensor([5, 5, big - 2, (1 << 32) + 62, big + 1, 7, big - 3], dtype=torch.int64)
+    qsl = torch.arange(rows + 1, dtype=torch.int32) * Q
+    req = torch.arange(rows, dtype=torch.int64)
+    bt = (torch.arange(rows * W, dtype=torch.int32) + 1).reshape(rows, W)
+    src = bt[:, 0].clone()
+    ctx.commit(acc, src, qsl, request_indices=req, block_table=bt, num_computed_tokens=computed,
+               mamba_block_size=bs)
+    arrays = dict(
+        src=src, qsl=qsl, request_indices=req, accepted=acc, spec_query_len=Q, block_table=bt,
+        num_computed=computed, block_size=bs, num_blocks=blocks,
+        commit_lens=ctx.commit_lens[:rows], final=ctx.final_state_indices[:rows],
+        boundary=ctx.boundary_state_indices[:rows], boundary_lens=ctx.boundary_recovery_lens[:rows],
+        valid=ctx.align_valid[:rows], col=ctx.align_col[:rows], history=hist, records0=records[0],
+        align=1, layout="packed", layers=1,
+        state_before0=states0[0], state_after0=states[0], conv_before0=convs0[0], conv_after0=convs[0],
+    )
+    _save(name, **arrays)
+
+
 def grouped_case(K, Gm, name, *, seed=2, D=32, H=2, HV=4, Q=4):
     """Two KV groups x two layers through ``GroupedCommitBucket.make_specs``:
     reordered requests, a null row, boundary crossings, an invalid group row,
@@ -396,6 +433,7 @@ def main(root):
     context_commit_case(K, "context_commit_align_packed", align=True, soa=False, seed=7)
     context_commit_case(K, "context_commit_align_soa", align=True, soa=True, layers=2, seed=8)
     grouped_case(K, Gm, "grouped_align_soa")
+    plan_int32_case(K, "context_plan_int32")
 
 
 if __name__ == "__main__":

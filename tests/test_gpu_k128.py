@@ -150,3 +150,50 @@ def test_verify_k128_matches_oracle(pkg, case):
                 assert np.array_equal(g_np[m], want[m]), "pre-normalised keys keep their input bits"
             else:
                 assert_fp32_close(g_np[m], want[m], what=name)
+
+
+def test_verify_k128_long_walks_alternating_live_and_null_rows(pkg):
+    """Many units per CTA (2048 rows x 8 value heads over the persistent
+    grid, ~37 units per CTA) with live, null, negative and out-of-pool slots
+    and empty windows interleaved at random, so that every CTA's walk switches
+    between its live and null paths many times: every unit's outputs and
+    records against the float64 restatement, null rows' outputs zero and their
+    records untouched."""
+    from tests.torch_reference import rel_errors_per_unit, rounded_ok, verify_rows
+
+    B, H, HV, Q, blocks = 2048, 2, 8, 4, 64
+    gen = torch.Generator().manual_seed(77)
+    kind = torch.randint(0, 10, (B,), generator=gen)
+    slots = 1 + torch.randint(0, blocks - 1, (B,), generator=gen)
+    slots = torch.where(kind < 3, torch.zeros_like(slots), slots)  # null
+    slots = torch.where(kind == 3, torch.full_like(slots, blocks), slots)  # out of pool
+    slots = torch.where(kind == 4, torch.full_like(slots, -2), slots)  # negative
+    qlen = torch.randint(0, Q + 1, (B,), generator=gen)
+    qlen = torch.where(kind == 5, torch.zeros_like(qlen), qlen)  # live slot, empty window
+    qsl = torch.cat([torch.zeros(1, dtype=torch.int64), torch.cumsum(qlen, 0)]).to(torch.int32)
+    T = int(qsl[-1])
+    unit = lambda x: x / x.norm(dim=-1, keepdim=True)  # noqa: E731
+    q = unit(torch.randn(1, T, H, D, generator=gen)).to(torch.bfloat16).cuda()
+    k = unit(torch.randn(1, T, H, D, generator=gen)).to(torch.bfloat16).cuda()
+    v = torch.randn(1, T, HV, D, generator=gen).to(torch.bfloat16).cuda()
+    g = (-torch.nn.functional.softplus(torch.randn(T, HV, generator=gen))).cuda()
+    beta = torch.sigmoid(torch.randn(T, HV, generator=gen)).cuda()
+    state = (torch.randn(blocks, HV, D, D, generator=gen) * 0.1).cuda()
+    records = torch.full((B, HV, Q, 2 * D + 1), -17.0, device="cuda")
+    out = torch.full((1, T, HV, D), -23.0, dtype=torch.bfloat16, device="cuda")
+    slots_d, qsl_d = slots.to(torch.int32).cuda(), qsl.cuda()
+    pkg.gdn_recoverssm_verify(g, beta, q, k, v, checkpoint_state=state, replay_cache=records, query_start_loc=qsl_d,
+                              state_indices=slots_d, spec_query_len=Q, out=out)
+    torch.cuda.synchronize()
+    assert int(torch.ops.gdn_recoverssm_ac.device_status()) == 0
+    res = verify_rows(q[0], k[0], v[0], g, beta, state, qsl_d, slots_d, Q=Q)
+    got_out = out[0][res["token"].clamp(0, T - 1)].float()  # [B, Q, HV, V]
+    want_out = torch.where(res["valid"][:, :, None, None], res["out"], torch.full_like(res["out"], float("nan")))
+    assert bool(rounded_ok(got_out, want_out, 7, -126).all()), "outputs"
+    null_rows = ~res["live"]
+    assert bool((got_out[null_rows][res["valid"][null_rows]] == 0).all()), "null rows must output zeros"
+    stored = ~torch.isnan(res["records"])
+    assert torch.equal(records != -17.0, stored), "record store mask"
+    emax, el2 = rel_errors_per_unit(records, res["records"], 2)
+    assert float(emax.max()) <= 1e-5 and float(el2.max()) <= 1e-5, (float(emax.max()), float(el2.max()))
+    assert int(null_rows.sum()) > 500 and int(res["live"].sum()) > 500

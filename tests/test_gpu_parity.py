@@ -270,6 +270,33 @@ def test_op_rejects_bad_arguments_before_launch(pkg):
                        [0] * 28, 1.0, 1)
 
 
+def test_fold_op_rejects_page_and_record_bounds_past_its_tensors(pkg):
+    """The fold bounds pages by config[5] and record rows by config[6]; the
+    op refuses values beyond the state pool / records it was given (and rows
+    beyond the plan capacity) before any launch."""
+    from gdn_recoverssm_b200 import synthetic
+
+    g = pkg
+    ops = torch.ops.gdn_recoverssm_ac
+    wl = synthetic.make(1, "cuda", seed=4, rows=8, pool=32, conv_dim=8)
+    ctx = g.GDNRecoverSSMCommitContext.from_tensors([wl.conv], [wl.state], [wl.records], spec_query_len=wl.Q,
+                                                    max_num_reqs=wl.B)
+    plan, fold = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=False)
+    plan.launch()
+    before = wl.state.clone()
+    for field, value, what in ((5, wl.state.shape[0] + 1, "page bound"), (6, wl.B + 1, "record rows"),
+                               (0, wl.B + 1, "plan capacity")):
+        cfg = list(fold.args[-2])
+        cfg[field] = value
+        with pytest.raises(RuntimeError, match="GDN RecoverSSM"):
+            ops.fold_ext(*fold.args[:-2], cfg, fold.args[-1])
+    torch.cuda.synchronize()
+    assert torch.equal(wl.state, before), "a refused fold launched"
+    fold.launch()
+    torch.cuda.synchronize()
+    assert not torch.equal(wl.state, before)
+
+
 @pytest.mark.parametrize("act", [torch.bfloat16, torch.float16])
 def test_reference_schema_ops_match_the_extended_ops(pkg, act):
     """The drop-ins for the reference's native ops -- gdn_recoverssm_ac::verify

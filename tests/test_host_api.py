@@ -30,6 +30,23 @@ def test_library_exports_every_declared_symbol():
     assert lib.gdn_rssm_abi_version() == 1
 
 
+def test_libraries_link_the_shared_cpp_runtime():
+    """Neither built library carries a private static C++ runtime: the torch
+    ops throw c10::Error through torch's own libstdc++, and a private copy's
+    iostreams crash while formatting a check's message."""
+    import shutil
+    import subprocess
+
+    from gdn_recoverssm_b200 import build
+
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm not available")
+    for lib in (build.CAPI_LIB, build.TORCH_LIB):
+        out = subprocess.run([nm, "-D", "--defined-only", str(lib)], capture_output=True, text=True).stdout
+        assert "__cxa_throw" not in out and "_ZNSt8ios_base4InitC" not in out, lib.name
+
+
 def test_torch_ops_register_reference_schemas():
     from gdn_recoverssm_b200 import _native
 

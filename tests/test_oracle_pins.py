@@ -256,7 +256,9 @@ def test_oracle_matches_reference_triton_verify(name):
             assert np.array_equal(recs[1][recs[1] != -16.0], _np(c["key"])[recs[1] != -16.0])
 
 
-CONTEXT_CASES = ["context_commit_none_packed", "context_commit_align_packed", "context_commit_align_soa"]
+CONTEXT_CASES = [
+    "context_commit_none_packed", "context_commit_align_packed", "context_commit_align_soa", "context_plan_int32",
+]
 
 
 def oracle_context_commit(c):
