@@ -66,6 +66,79 @@ def _traffic_profile(cfg, reduced):
 
 
 class ClockSampler:
+    """SM clock and clock-event reasons of one GPU, sampled every millisecond
+    through NVML on a background thread while the timed passes run (falls
+    back to ``nvidia-smi -lms 200`` without NVML)."""
+
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("sw_power_cap", 0x4))
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []  # (sm MHz, power W, reason bits)
+        self.max_mhz = None
+        self.source = "nvml"
+        self._stop = None
+        self._thread = None
+        self._smi = None
+
+    def _handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.device)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+
+    def __enter__(self):
+        import threading
+
+        try:
+            nv, h = self._handle()
+        except Exception:
+            self.source = "nvidia-smi"
+            self._smi = _SmiSampler(self.device.index or 0).__enter__()
+            return self
+        self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                      nv.nvmlDeviceGetPowerUsage(h) / 1000.0, int(reasons(h))))
+                except Exception:
+                    pass
+                self._stop.wait(0.001)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._smi is not None:
+            self._smi.__exit__(*exc)
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+
+    def summary(self):
+        if self._smi is not None:
+            return self._smi.summary()
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"], "source": self.source}
+        active = sorted({name for _, _, bits in self.rows for name, bit in self.REASONS if bits & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": active, "samples": len(self.rows), "sm_mhz_min": min(r[0] for r in self.rows),
+                "power_w_max": max(r[1] for r in self.rows), "source": "nvml, every 1 ms over the timed passes"}
+
+
+class _SmiSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -111,7 +184,8 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+                "samples": len(rows), "source": "nvidia-smi, every 200 ms",
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
 def _dist():
@@ -166,6 +240,42 @@ def cpu_baseline(cfg, *, rows_sample, seed=0, repeats=1, gated=False):
     return {"value": B / t, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"config {cfg}: {B} of {spec['B']} rows x {HV} value heads, verify + fold, best of {repeats}",
             "seconds_per_sample": t}
+
+
+def numpy_oracle_baseline(cfg, *, units_sample=1024, seed=0):
+    """Time the float64 NumPy restatement of the reference's math oracle --
+    ``verify_records`` + ``commit`` of plugin/tests/test_math_oracle.py:56-92,
+    as oracle/gdn_oracle.py restates them -- looped over a seeded sample of
+    (row, value head) units of the configuration in one process, and
+    extrapolate to the whole batch (every unit costs the same)."""
+    import numpy as np
+
+    from gdn_recoverssm_b200 import synthetic
+    from oracle import gdn_oracle as O
+
+    spec = synthetic.CONFIGS[cfg]
+    B, HV, D, Q = spec["B"], spec["HV"], spec["D"], spec["Q"]
+    rng = np.random.default_rng(seed)
+    n = min(units_sample, B * HV)
+    unit = lambda x: x / np.linalg.norm(x, axis=-1, keepdims=True)  # noqa: E731
+    cases = [(rng.standard_normal((D, D)) * 0.1, unit(rng.standard_normal((Q, D))), unit(rng.standard_normal((Q, D))),
+              rng.standard_normal((Q, D)), -np.log1p(np.exp(rng.standard_normal(Q))),
+              1.0 / (1.0 + np.exp(-rng.standard_normal(Q))), int(rng.integers(1, Q + 1))) for _ in range(n)]
+    t0 = time.perf_counter()
+    for state, q, k, v, g, beta, acc in cases:
+        _, recs = O.verify_records(state, q, k, v, g, beta, D**-0.5)
+        O.commit(state, recs, acc)
+    per_unit = (time.perf_counter() - t0) / n
+    try:
+        from threadpoolctl import threadpool_info
+
+        blas = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"), default=1)
+    except Exception:  # pragma: no cover
+        blas = None
+    return {"value": 1.0 / (per_unit * HV), "unit": UNIT, "cores": 1, "blas_threads": blas, "kind": "port",
+            "sample": f"config {cfg}: {n} of {B * HV} (row, value head) units, float64 verify_records + commit "
+                      f"per unit in one process, extrapolated to the batch",
+            "seconds_per_unit": per_unit}
 
 
 def run_reference(args):
@@ -275,7 +385,7 @@ def run_b200(args):
     bnd = ((ctx.boundary_state_indices[: wl.B] > 0) & (ctx.boundary_recovery_lens[: wl.B] > 0)
            & (ctx.boundary_state_indices[: wl.B] != ctx.final_state_indices[: wl.B])).cpu()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         barrier()
         # the step as a serving loop issues it: nothing between the launches
         # (the fold is a programmatic dependent of the plan)
@@ -357,6 +467,8 @@ def run_b200(args):
         line["config"]["commit_conv"] = f"conv history compacted in the commit: {args.conv_dim} channels"
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(args.config, rows_sample=args.cpu_rows, gated=args.gated)
+        line["cpu_baseline"]["nproc"] = os.cpu_count()
+        line["cpu_baseline"]["numpy_oracle"] = numpy_oracle_baseline(args.config)
     print(json.dumps(line))
     return 0
 
@@ -397,7 +509,7 @@ def _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=3):
     out_dev = [torch.empty_like(wl.out) for _ in range(nbuf)]
     out_host = [torch.empty(wl.out.shape, dtype=wl.out.dtype).pin_memory() for _ in range(nbuf)]
     d2h = out_host[0].numel() * out_host[0].element_size()
-    steps = max(4, args.steps // 4)
+    steps = max(args.e2e_steps, args.steps)
     h2d_stream = torch.cuda.Stream(dev)
     d2h_stream = torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(nbuf)]    # inputs of buffer b on the device
@@ -465,6 +577,7 @@ def main(argv=None):
     ap.add_argument("--gated", action="store_true",
                     help="verify through the fused-gating entry point (raw a, b, A_log, dt_bias)")
     ap.add_argument("--e2e-buffers", type=int, default=3, help="device input/output buffers of the end-to-end loop")
+    ap.add_argument("--e2e-steps", type=int, default=50, help="fewest steps the end-to-end pass times")
     ap.add_argument("--rows", type=int, default=None, help="reduced batch (profiling cases only)")
     ap.add_argument("--pool", type=int, default=None, help="reduced state pool (profiling cases only)")
     args = ap.parse_args(argv)

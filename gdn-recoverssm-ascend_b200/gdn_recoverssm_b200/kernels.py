@@ -28,6 +28,7 @@ from typing import Any, Callable
 import torch
 
 from . import _native
+from .tables import LayerTables
 
 NULL_BLOCK_ID = 0  # page 0 is the null page
 MAX_SPEC_QUERY_LEN = 8  # window bound of every kernel (kernels.py:101)
@@ -46,14 +47,6 @@ def _require(cond: bool, msg: str) -> None:
     reference's message format (kernels.py:143-151)."""
     if not cond:
         raise ValueError(f"GDN RecoverSSM: {msg}")
-
-
-def _ptr_table(tensors: Sequence[torch.Tensor], device) -> torch.Tensor:
-    """int64 table of data pointers keeping each uint64 bit pattern (pointers
-    with the top bit set would overflow a plain int64 conversion)."""
-    ptrs = [t.data_ptr() for t in tensors]
-    ptrs = [p if p < (1 << 63) else p - (1 << 64) for p in ptrs]
-    return torch.tensor(ptrs, dtype=torch.int64, device=device)
 
 
 @dataclass
@@ -365,142 +358,128 @@ def _verify(g, beta, q, k, v, checkpoint_state, replay_cache, query_start_loc, s
 # --------------------------------------------------------------------------- #
 # per-context commit
 # --------------------------------------------------------------------------- #
-@dataclass
-class GDNRecoverSSMCommitContext:
-    """Per-layer-set commit state: address/stride tables of every layer's
-    checkpoint pool, conv pool and records, plus reusable plan buffers
-    (kernels.py:1399-2052).  Build with ``from_tensors``."""
+_PLAN_ROWS = ("commit_lens", "final_state_indices", "boundary_state_indices", "boundary_recovery_lens",
+              "align_valid", "align_col")
 
-    conv_states: tuple
-    conv_state_base_addrs: torch.Tensor
-    conv_state_block_strides: torch.Tensor
-    conv_state_dim_strides: torch.Tensor
-    conv_state_token_strides: torch.Tensor
-    conv_history_len: int
-    checkpoints: tuple
-    state_base_addrs: torch.Tensor
-    state_block_strides: torch.Tensor
-    replays: tuple
-    replay_base_addrs: torch.Tensor
-    replay_block_strides: torch.Tensor
-    commit_lens: torch.Tensor
-    final_state_indices: torch.Tensor
-    boundary_state_indices: torch.Tensor
-    boundary_recovery_lens: torch.Tensor
-    spec_query_len: int
-    num_blocks: int
+
+def _same_layout(tensors, signature) -> bool:
+    """Every tensor has the first one's ``signature``."""
+    first = signature(tensors[0])
+    return all(signature(t) == first for t in tensors[1:])
+
+
+def _record_planes(replays, num_value_heads, value_dim, key_dim, window, device):
+    """The correction / key / decay plane of every layer's records and the key
+    head count, after checking that all layers share one record geometry
+    (packed fp32 ``[R, HV, Q, V + K + 1]`` or typed SoA buffers)."""
+    typed = [isinstance(r, ReplayRecordBuffers) for r in replays]
+    _require(all(typed) or not any(typed), "packed and typed records cannot share a commit context")
+    if not typed[0]:
+        ok = all(r.ndim == 4 for r in replays) and _same_layout(
+            replays, lambda r: (tuple(r.shape), r.dtype, r.stride()[1:], r.device))
+        r0 = replays[0]
+        ok = ok and tuple(r0.shape[1:]) == (num_value_heads, window, value_dim + key_dim + 1)
+        ok = ok and r0.dtype == torch.float32 and r0.device == device
+        _require(ok, "layers need matching packed FP32 replay buffers")
+        planes = tuple(replays)
+        return planes, planes, planes, num_value_heads
+    corrs = tuple(r.correction for r in replays)
+    keys = tuple(r.key for r in replays)
+    decays = tuple(r.decay for r in replays)
+    heads = int(keys[0].shape[1])
+    _require(heads > 0 and num_value_heads % heads == 0, "record key heads are incompatible")
+    rows = int(corrs[0].shape[0])
+    expected = ((rows, num_value_heads, window, value_dim), (rows, heads, window, key_dim),
+                (rows, num_value_heads, window))
+    ok = all(
+        (tuple(c.shape), tuple(k.shape), tuple(d.shape)) == expected and all(t.device == device for t in (c, k, d))
+        for c, k, d in zip(corrs, keys, decays)
+    )
+    ok = ok and all(c.dtype == torch.float32 and d.dtype == torch.float32 for c, d in zip(corrs, decays))
+    ok = ok and keys[0].dtype in (torch.float16, torch.bfloat16, torch.float32)
+    ok = ok and all(_same_layout(p, lambda t: (t.dtype, t.stride()[1:])) for p in (corrs, keys, decays))
+    _require(ok, "layers need matching typed replay geometry/dtypes/strides")
+    return corrs, keys, decays, heads
+
+
+class GDNRecoverSSMCommitContext:
+    """Commit state of one set of GDN layers (kernels.py:1399-2052): the
+    layers' checkpoint pools, conv pools and records, their per-layer address
+    and stride tables (one device tensor, ``tables.LayerTables``) and the
+    reusable plan buffers (one int32 tensor, a row per plan array).  Build it
+    with ``from_tensors``; the attribute names are the reference's, since the
+    serving code and the grouped commit read them."""
+
+    def __init__(self, *, conv_states, checkpoints, replays, planes, num_key_heads, spec_query_len, conv_history_len,
+                 max_num_reqs):
+        device = checkpoints[0].device
+        corrs, keys, decays = planes
+        self.checkpoints = tuple(checkpoints)
+        self.conv_states = tuple(conv_states)
+        self.replays = tuple(replays)
+        self.records = list(replays)
+        self.spec_query_len = int(spec_query_len)
+        self.conv_history_len = int(conv_history_len)
+        self.num_blocks = int(checkpoints[0].shape[0])
+        self.num_key_heads = int(num_key_heads)
+        self.record_layout = "soa" if isinstance(replays[0], ReplayRecordBuffers) else "packed"
+        self.record_rows = int(corrs[0].shape[0])
+        self.key_dtype = keys[0].dtype
+        self.record_bytes = sum(record_nbytes(r) for r in replays)
+        self.tables = LayerTables(device, (self.checkpoints, self.conv_states, corrs, keys, decays))
+        self.plan = torch.zeros(len(_PLAN_ROWS), max_num_reqs, dtype=torch.int32, device=device)
+        self.layer_groups = torch.zeros(len(self.checkpoints), dtype=torch.int32, device=device)
+
+    # per-layer tables (row views of self.tables)
+    state_base_addrs = property(lambda self: self.tables["state_addr"])
+    state_block_strides = property(lambda self: self.tables["state_block"])
+    conv_state_base_addrs = property(lambda self: self.tables["conv_addr"])
+    conv_state_block_strides = property(lambda self: self.tables["conv_block"])
+    conv_state_dim_strides = property(lambda self: self.tables["conv_dim"])
+    conv_state_token_strides = property(lambda self: self.tables["conv_token"])
+    correction_base_addrs = replay_base_addrs = property(lambda self: self.tables["corr_addr"])
+    correction_block_strides = replay_block_strides = property(lambda self: self.tables["corr_block"])
+    key_base_addrs = property(lambda self: self.tables["key_addr"])
+    key_block_strides = property(lambda self: self.tables["key_block"])
+    decay_base_addrs = property(lambda self: self.tables["decay_addr"])
+    decay_block_strides = property(lambda self: self.tables["decay_block"])
+    # plan buffers (row views of self.plan)
+    commit_lens = property(lambda self: self.plan[0])
+    final_state_indices = property(lambda self: self.plan[1])
+    boundary_state_indices = property(lambda self: self.plan[2])
+    boundary_recovery_lens = property(lambda self: self.plan[3])
+    align_valid = property(lambda self: self.plan[4])
+    align_col = property(lambda self: self.plan[5])
 
     @classmethod
     def from_tensors(cls, conv_states, checkpoints, replays, *, spec_query_len: int, max_num_reqs: int,
                      conv_dim_first: bool = True) -> "GDNRecoverSSMCommitContext":
-        """Validate every layer's page layout and build the int64 address /
-        stride tables and plan buffers (kernels.py:1421-1565)."""
-        _require(len(checkpoints) > 0, "commit requires at least one layer")
-        _require(len(conv_states) == len(checkpoints) == len(replays), "conv, state and replay lists differ")
+        """Check that every layer shares one page layout and bind the layers
+        (kernels.py:1421-1565): checkpoints ``[blocks, HV, V, K]``, conv pools
+        ``[blocks, dim, window]`` (or ``[blocks, window, dim]`` with
+        ``conv_dim_first=False``) with window = history + Q - 1, and packed or
+        typed records.  The kernels take raw pointers, so nothing here is
+        trusted later."""
+        layers = len(checkpoints)
+        _require(layers > 0, "commit requires at least one layer")
+        _require(len(conv_states) == layers == len(replays), "conv, state and replay lists differ")
         _require(0 < spec_query_len <= MAX_SPEC_QUERY_LEN, f"spec_query_len must be in [1, {MAX_SPEC_QUERY_LEN}]")
-        if not conv_dim_first:
-            conv_states = [s.transpose(-1, -2) for s in conv_states]
-        ref = checkpoints[0]
-        _require(ref.ndim == 4, "checkpoint must be four-dimensional")
-        nb, HV, V, K = ref.shape
-        dev = ref.device
-        for s in checkpoints:
-            _require(
-                s.shape == ref.shape and s.dtype == ref.dtype and s.stride()[1:] == ref.stride()[1:] and s.device == dev,
-                "layers need matching checkpoints",
-            )
-        soa = isinstance(replays[0], ReplayRecordBuffers)
-        _require(all(isinstance(r, ReplayRecordBuffers) == soa for r in replays),
-                 "packed and typed records cannot share a commit context")
-        if soa:
-            corrs = [r.correction for r in replays]
-            keys = [r.key for r in replays]
-            decays = [r.decay for r in replays]
-            H = keys[0].shape[1]
-            _require(H > 0 and HV % H == 0, "record key heads are incompatible")
-            for c, k, d in zip(corrs, keys, decays):
-                _require(
-                    c.shape == corrs[0].shape
-                    and tuple(c.shape[1:]) == (HV, spec_query_len, V)
-                    and tuple(k.shape) == (c.shape[0], H, spec_query_len, K)
-                    and tuple(d.shape) == (c.shape[0], HV, spec_query_len)
-                    and c.dtype == d.dtype == torch.float32
-                    and k.dtype in (torch.float16, torch.bfloat16, torch.float32)
-                    and k.dtype == keys[0].dtype
-                    and all(t.device == dev for t in (c, k, d))
-                    and c.stride()[1:] == corrs[0].stride()[1:]
-                    and k.stride()[1:] == keys[0].stride()[1:]
-                    and d.stride()[1:] == decays[0].stride()[1:],
-                    "layers need matching typed replay geometry/dtypes/strides",
-                )
-        else:
-            corrs = keys = decays = list(replays)
-            H = HV
-            for r in replays:
-                _require(
-                    r.ndim == 4
-                    and tuple(r.shape[1:]) == (HV, spec_query_len, V + K + 1)
-                    and r.shape == replays[0].shape
-                    and r.dtype == torch.float32
-                    and r.stride()[1:] == replays[0].stride()[1:]
-                    and r.device == dev,
-                    "layers need matching packed FP32 replay buffers",
-                )
-        conv_ref = conv_states[0]
-        _require(conv_ref.ndim == 3 and conv_ref.shape[0] == nb,
+        convs = [c if conv_dim_first else c.transpose(-1, -2) for c in conv_states]
+        _require(checkpoints[0].ndim == 4, "checkpoint must be four-dimensional")
+        blocks, value_heads, value_dim, key_dim = checkpoints[0].shape
+        device = checkpoints[0].device
+        _require(_same_layout(checkpoints, lambda s: (tuple(s.shape), s.dtype, s.stride()[1:], s.device)),
+                 "layers need matching checkpoints")
+        corrs, keys, decays, heads = _record_planes(replays, value_heads, value_dim, key_dim, spec_query_len, device)
+        _require(convs[0].ndim == 3 and convs[0].shape[0] == blocks,
                  "conv state must be [blocks, dim, window] with the checkpoint's block count")
-        for c in conv_states:
-            _require(
-                c.shape == conv_ref.shape and c.dtype == conv_ref.dtype and c.stride()[1:] == conv_ref.stride()[1:]
-                and c.device == dev,
-                "layers need matching conv states",
-            )
-        conv_dim, conv_len = conv_ref.shape[1:]
-        hist = conv_len - spec_query_len + 1
-        _require(hist > 0, "conv state is shorter than its window")
-
-        def strides(ts, dim):
-            return torch.tensor([t.stride(dim) for t in ts], dtype=torch.int64, device=dev)
-
-        def plan_buf():
-            return torch.zeros(max_num_reqs, dtype=torch.int32, device=dev)
-
-        context = cls(
-            tuple(conv_states),
-            _ptr_table(conv_states, dev),
-            strides(conv_states, 0),
-            strides(conv_states, 1),
-            strides(conv_states, 2),
-            hist,
-            tuple(checkpoints),
-            _ptr_table(checkpoints, dev),
-            strides(checkpoints, 0),
-            tuple(replays),
-            _ptr_table(corrs, dev),
-            strides(corrs, 0),
-            plan_buf(),
-            plan_buf(),
-            plan_buf(),
-            plan_buf(),
-            spec_query_len,
-            nb,
-        )
-        context.records = list(replays)
-        context.record_rows = int(corrs[0].shape[0])
-        context.record_layout = "soa" if soa else "packed"
-        context.num_key_heads = int(H)
-        context.key_dtype = keys[0].dtype
-        context.correction_base_addrs = context.replay_base_addrs
-        context.correction_block_strides = context.replay_block_strides
-        context.key_base_addrs = _ptr_table(keys, dev)
-        context.key_block_strides = strides(keys, 0)
-        context.decay_base_addrs = _ptr_table(decays, dev)
-        context.decay_block_strides = strides(decays, 0)
-        context.record_bytes = sum(record_nbytes(r) for r in replays)
-        context.align_valid = plan_buf()
-        context.align_col = plan_buf()
-        context.layer_groups = torch.zeros(len(checkpoints), dtype=torch.int32, device=dev)
-        return context
+        _require(_same_layout(convs, lambda c: (tuple(c.shape), c.dtype, c.stride()[1:])) and all(
+            c.device == device for c in convs), "layers need matching conv states")
+        history = int(convs[0].shape[2]) - spec_query_len + 1
+        _require(history > 0, "conv state is shorter than its window")
+        return cls(conv_states=convs, checkpoints=checkpoints, replays=replays, planes=(corrs, keys, decays),
+                   num_key_heads=heads, spec_query_len=spec_query_len, conv_history_len=history,
+                   max_num_reqs=max_num_reqs)
 
     def make_commit_specs(self, num_accepted_tokens, state_indices, query_start_loc, request_indices=None,
                           block_table=None, num_computed_tokens=None, mamba_block_size=None,

@@ -13,8 +13,6 @@ valid as long as it lives.
 
 from __future__ import annotations
 
-from collections.abc import Sequence
-
 import torch
 
 # row name -> (plane, what): plane indexes the tensors given to LayerTables,
@@ -40,11 +38,6 @@ def as_int64_bits(addr: int) -> int:
     """A data pointer as the int64 holding the same 64 bits (addresses with the
     top bit set would overflow a plain conversion)."""
     return addr - (1 << 64) if addr >= (1 << 63) else addr
-
-
-def pointer_table(tensors: Sequence[torch.Tensor], device) -> torch.Tensor:
-    """int64 device tensor of the data pointers of ``tensors`` (bit patterns kept)."""
-    return torch.tensor([as_int64_bits(t.data_ptr()) for t in tensors], dtype=torch.int64, device=device)
 
 
 class LayerTables:
