@@ -54,14 +54,14 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _traffic_profile(cfg, reduced):
-    """Per-launch DRAM traffic (bytes) of the fold kernel at this config's full
-    size, from the committed ncu summary; None for reduced workloads or when
-    no capture exists."""
+def _traffic_profile(key, reduced):
+    """Per-launch DRAM traffic (bytes) of the named kernel at a config's full
+    size (``key`` = "<kernel>_config<N>"), from the committed ncu summaries;
+    None for reduced workloads or when no capture exists."""
     p = ROOT / "profiles" / "traffic.json"
     if reduced or not p.exists():
         return None
-    entry = json.loads(p.read_text()).get(f"fold_config{cfg}")
+    entry = json.loads(p.read_text()).get(key)
     return int(entry) if entry is not None else None
 
 
@@ -344,7 +344,9 @@ def run_b200(args):
 
     _native.ops()
     conv = args.conv_dim > 0
-    wl = synthetic.make(args.config, dev, seed=0, world=world, rank=rank, conv_dim=args.conv_dim if conv else 16,
+    shard_world, shard_rank = (args.shard_of, 0) if args.shard_of else (world, rank)
+    wl = synthetic.make(args.config, dev, seed=0, world=shard_world, rank=shard_rank,
+                        conv_dim=args.conv_dim if conv else 16,
                         rows=args.rows, pool=args.pool,
                         gated=args.gated)
     stream = torch.cuda.current_stream(dev)
@@ -367,8 +369,7 @@ def run_b200(args):
                                     spec_query_len=wl.Q, out=wl.out)
 
     specs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=conv, **align_kw)
-    plan_spec, fold_spec = specs[0], specs[-1]
-    conv_spec = specs[1] if conv else None
+    names = [sp.name for sp in specs]  # commit_plan, (compact_conv,) fold
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -384,17 +385,17 @@ def run_b200(args):
     lens = ctx.commit_lens[: wl.B].cpu()
     bnd = ((ctx.boundary_state_indices[: wl.B] > 0) & (ctx.boundary_recovery_lens[: wl.B] > 0)
            & (ctx.boundary_state_indices[: wl.B] != ctx.final_state_indices[: wl.B])).cpu()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2 + len(specs))] for _ in range(args.steps)]
     with ClockSampler(dev) as clocks:
         barrier()
         # the step as a serving loop issues it: nothing between the launches
-        # (the fold is a programmatic dependent of the plan)
+        # (each commit launch is a programmatic dependent of the kernel before it)
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
         for i in range(args.steps):
             verify()
-            for sp in specs:  # plan, (conv compaction,) fold
+            for sp in specs:
                 sp.launch()
         t_end.record(stream)
         barrier()
@@ -404,26 +405,19 @@ def run_b200(args):
             e[0].record(stream)
             verify()
             e[1].record(stream)
-            plan_spec.launch()
-            e[2].record(stream)
-            if conv_spec is not None:
-                conv_spec.launch()
-            e[3].record(stream)
-            fold_spec.launch()
-            e[4].record(stream)
+            for j, sp in enumerate(specs):
+                sp.launch()
+                e[2 + j].record(stream)
         barrier()
         # end to end through the public API with host buffers
         e2e = _e2e(g, wl, ctx, align_kw, args, dev, stream, barrier, nbuf=args.e2e_buffers)
     total_ms = t_start.elapsed_time(t_end)
-    verify_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
-    plan_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
-    conv_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
-    fold_ms = sum(e[3].elapsed_time(e[4]) for e in ev) / args.steps
+    split = [sum(e[k].elapsed_time(e[k + 1]) for e in ev) / args.steps for k in range(1 + len(specs))]
     step_ms = total_ms / args.steps
     from gdn_recoverssm_b200.sharding import max_over_ranks
 
-    step_ms, verify_ms, plan_ms, conv_ms, fold_ms, e2e_ms = max_over_ranks(
-        [step_ms, verify_ms, plan_ms, conv_ms, fold_ms, e2e["ms"]], device=dev)
+    timings = max_over_ranks([step_ms, e2e["ms"], *split], device=dev)
+    step_ms, e2e_ms, verify_ms, spec_ms = timings[0], timings[1], timings[2], dict(zip(names, timings[3:]))
     clk = clocks.summary()
     status = int(torch.ops.gdn_recoverssm_ac.device_status())
     if world > 1:
@@ -434,11 +428,20 @@ def run_b200(args):
     peak, peak_kind = _peaks()
     vbytes = synthetic.verify_bytes(wl)
     fbytes = synthetic.commit_bytes(wl, lens, int(bnd.sum()))
-    fold_gbs = fbytes / (fold_ms * 1e-3) / 1e9
-    verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
     cbytes = synthetic.conv_bytes(wl, lens, int(bnd.sum()), ctx.conv_history_len) if conv else 0
+    verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
     step_gbs = (vbytes + fbytes + cbytes) / (step_ms * 1e-3) / 1e9
-    traffic = _traffic_profile(args.config, args.rows is not None or args.pool is not None)
+    kernels = {"verify": {"ms": verify_ms, "bytes": vbytes, "GB/s": verify_gbs, "frac": verify_gbs / peak}}
+    bytes_of = {"fold": fbytes, "compact_conv": cbytes}
+    for name, ms in spec_ms.items():
+        kernels[name] = {"ms": ms}
+        if name in bytes_of:
+            gbs = bytes_of[name] / (ms * 1e-3) / 1e9
+            kernels[name].update({"bytes": bytes_of[name], "GB/s": gbs, "frac": gbs / peak})
+    kernels["step"] = {"GB/s": step_gbs, "frac": step_gbs / peak, "per_rank_bytes": vbytes + fbytes + cbytes}
+    top = "fold"  # the largest byte mover
+    reduced = args.rows is not None or args.pool is not None or bool(args.shard_of) or conv
+    traffic = _traffic_profile(f"{top}_config{args.config}", reduced)
     if traffic is not None:
         traffic = int(traffic * wl.units / (synthetic.CONFIGS[args.config]["B"] * synthetic.CONFIGS[args.config]["HV"]))
     value = wl.B / (step_ms * 1e-3)
@@ -448,22 +451,18 @@ def run_b200(args):
         "data": "synthetic", "config": _config_dict(args.config, world, args.gated),
         "e2e": {"value": wl.B / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e_ms},
-        "roofline": {"bound": "hbm", "kernel": "fold (grouped commit)", "achieved": fold_gbs, "peak": peak,
-                     "unit": "GB/s", "frac": fold_gbs / peak, "peak_kind": peak_kind,
-                     "traffic": traffic, "algorithmic_bytes_per_launch": fbytes},
-        "kernels": {
-            "verify": {"ms": verify_ms, "bytes": vbytes, "GB/s": verify_gbs, "frac": verify_gbs / peak},
-            "commit_plan": {"ms": plan_ms},
-            "fold": {"ms": fold_ms, "bytes": fbytes, "GB/s": fold_gbs, "frac": fold_gbs / peak},
-            "step": {"GB/s": step_gbs, "frac": step_gbs / peak, "per_rank_bytes": vbytes + fbytes + cbytes},
-        },
-        "gpu_launches": (4 if conv else 3) * args.steps * world,  # verify, plan, (conv,) fold per step and rank
+        "roofline": {"bound": "hbm", "kernel": "fold (grouped commit)",
+                     "achieved": kernels[top]["GB/s"], "peak": peak, "unit": "GB/s", "frac": kernels[top]["frac"],
+                     "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": bytes_of[top]},
+        "kernels": kernels,
+        "gpu_launches": (1 + len(specs)) * args.steps * world,  # verify + the commit launches, per step and rank
         "clocks": clk,
         "device_status": status,
     }
+    line["config"]["commit_launches"] = names
+    if args.shard_of:
+        line["config"]["parallelism"] = f"rank 0 of a {args.shard_of}-way v-head split, on one GPU (profiling only)"
     if conv:
-        conv_gbs = cbytes / (conv_ms * 1e-3) / 1e9
-        line["kernels"]["compact_conv"] = {"ms": conv_ms, "bytes": cbytes, "GB/s": conv_gbs, "frac": conv_gbs / peak}
         line["config"]["commit_conv"] = f"conv history compacted in the commit: {args.conv_dim} channels"
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(args.config, rows_sample=args.cpu_rows, gated=args.gated)
@@ -579,6 +578,8 @@ def main(argv=None):
     ap.add_argument("--e2e-buffers", type=int, default=3, help="device input/output buffers of the end-to-end loop")
     ap.add_argument("--e2e-steps", type=int, default=50, help="fewest steps the end-to-end pass times")
     ap.add_argument("--rows", type=int, default=None, help="reduced batch (profiling cases only)")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="one GPU runs rank 0's head shard of an N-way split (profiling the per-rank step only)")
     ap.add_argument("--pool", type=int, default=None, help="reduced state pool (profiling cases only)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "b200":

@@ -255,17 +255,25 @@ int gdn_rssm_verify_gated(const void *q, const void *k, const void *v, const voi
                      value_dim, flags, A_log, dt_bias, softplus_beta, softplus_threshold, stream);
 }
 
-int gdn_rssm_fold(const int64_t *state_addrs, const int64_t *state_block_strides, const int64_t *corr_addrs,
-                  const int64_t *corr_block_strides, const int64_t *key_addrs, const int64_t *key_block_strides,
-                  const int64_t *decay_addrs, const int64_t *decay_block_strides, const int32_t *layer_groups,
-                  gdn_rssm_index_view source, const int32_t *lengths, const int32_t *final_indices,
-                  const int32_t *boundary_indices, const int32_t *boundary_lengths, int64_t plan_len,
-                  const int64_t *config, int64_t config_len, int32_t state_dtype, int32_t key_dtype, int32_t key_dim,
-                  int32_t value_dim, uint32_t flags, void *stream) {
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Validation of the commit-side arguments, shared by the separate entry points
+// and the fused ones: each fills its parameter block or returns the error.
+// ---------------------------------------------------------------------------
+namespace gdn_rssm {
+
+// The fold's configuration and per-layer tables (everything but the plan).
+static int prepare_fold(FoldParams &p, const int64_t *state_addrs, const int64_t *state_block_strides,
+                        const int64_t *corr_addrs, const int64_t *corr_block_strides, const int64_t *key_addrs,
+                        const int64_t *key_block_strides, const int64_t *decay_addrs,
+                        const int64_t *decay_block_strides, const int32_t *layer_groups, const int64_t *config,
+                        int64_t config_len, int32_t state_dtype, int32_t key_dtype, int32_t key_dim,
+                        int32_t value_dim, uint32_t flags) {
   GDN_REQUIRE(config != nullptr && config_len == GDN_RSSM_FOLD_FIELDS, "fold config must have 17 fields");
   int64_t f[GDN_RSSM_FOLD_FIELDS];
   std::memcpy(f, config, sizeof(f));
-  FoldParams p{};
+  p = FoldParams{};
   p.rows = f[0];
   p.layers = f[1];
   p.heads = f[2];
@@ -298,12 +306,10 @@ int gdn_rssm_fold(const int64_t *state_addrs, const int64_t *state_block_strides
   GDN_REQUIRE(p.query_len >= 1 && p.query_len <= kMaxWindow, "spec_query_len must be in [1, 8]");
   GDN_REQUIRE(p.layers * p.rows * p.heads < (int64_t(1) << 31), "fold launch grid too large");
   if (p.rows == 0) return GDN_RSSM_OK;
-  GDN_REQUIRE(state_addrs && state_block_strides && corr_addrs && corr_block_strides && layer_groups && lengths &&
-                  final_indices && boundary_indices && boundary_lengths && plan_len > 0,
+  GDN_REQUIRE(state_addrs && state_block_strides && corr_addrs && corr_block_strides && layer_groups,
               "fold table pointer is null");
   GDN_REQUIRE(packed || (key_addrs && key_block_strides && decay_addrs && decay_block_strides),
               "typed records need key and decay tables");
-  GDN_REQUIRE(view_ok(source), "fold source indices must be an int32/int64 view");
   const int64_t epc = 16 / host_dtype_size(state_dtype);
   GDN_REQUIRE(p.state_hs % epc == 0 && p.state_vs % epc == 0 && p.state_vs >= key_dim,
               "state head / row strides must be 16-byte aligned with contiguous K rows");
@@ -316,22 +322,17 @@ int gdn_rssm_fold(const int64_t *state_addrs, const int64_t *state_block_strides
   p.decay_addrs = decay_addrs;
   p.decay_bs = decay_block_strides;
   p.layer_groups = layer_groups;
-  p.source = source;
-  p.lengths = lengths;
-  p.finals = final_indices;
-  p.boundaries = boundary_indices;
-  p.boundary_lens = boundary_lengths;
-  p.plan_len = plan_len;
   p.flags = flags;
-  return launch_fold(p, key_dim, state_dtype, packed ? GDN_RSSM_F32 : key_dtype, static_cast<cudaStream_t>(stream));
+  return GDN_RSSM_OK;
 }
 
-int gdn_rssm_commit_plan(gdn_rssm_index_view num_accepted, gdn_rssm_index_view request_indices,
-                         gdn_rssm_index_view state_indices, gdn_rssm_index_view query_start_loc,
-                         gdn_rssm_table_view block_table, gdn_rssm_index_view num_computed, int32_t *commit_lens,
-                         int32_t *final_indices, int32_t *boundary_indices, int32_t *boundary_lengths,
-                         int32_t *align_valid, int32_t *align_col, int64_t rows, int64_t spec_query_len,
-                         int64_t num_blocks, int64_t block_size, int64_t null_block, void *stream) {
+static int prepare_commit_plan(CommitPlanParams &p, gdn_rssm_index_view num_accepted,
+                               gdn_rssm_index_view request_indices, gdn_rssm_index_view state_indices,
+                               gdn_rssm_index_view query_start_loc, gdn_rssm_table_view block_table,
+                               gdn_rssm_index_view num_computed, int32_t *commit_lens, int32_t *final_indices,
+                               int32_t *boundary_indices, int32_t *boundary_lengths, int32_t *align_valid,
+                               int32_t *align_col, int64_t rows, int64_t spec_query_len, int64_t num_blocks,
+                               int64_t block_size, int64_t null_block) {
   GDN_REQUIRE(null_block == 0, "the null block id must be 0 (page zero is reserved)");
   GDN_REQUIRE(rows >= 0 && spec_query_len >= 1 && spec_query_len <= kMaxWindow, "plan geometry");
   if (rows == 0) return GDN_RSSM_OK;
@@ -352,7 +353,7 @@ int gdn_rssm_commit_plan(gdn_rssm_index_view num_accepted, gdn_rssm_index_view r
     GDN_REQUIRE(block_size < (int64_t{1} << 31) && block_table.cols < (int64_t{1} << 31),
                 "align block size and block table width must stay below 2^31");
   }
-  CommitPlanParams p{};
+  p = CommitPlanParams{};
   p.accepted = num_accepted;
   p.request = request_indices;
   p.state = state_indices;
@@ -370,15 +371,15 @@ int gdn_rssm_commit_plan(gdn_rssm_index_view num_accepted, gdn_rssm_index_view r
   p.num_blocks = num_blocks;
   p.block_size = align ? block_size : 1;
   p.null_block = null_block;
-  return launch_commit_plan(p, static_cast<cudaStream_t>(stream));
+  return GDN_RSSM_OK;
 }
 
-int gdn_rssm_grouped_plan(gdn_rssm_index_view sampled, const gdn_rssm_plan_group *groups, int32_t num_groups,
-                          int32_t *source, int32_t *length, int32_t *final_indices, int32_t *boundary_indices,
-                          int32_t *boundary_lengths, int32_t *valid, int32_t *col, gdn_rssm_index_view idx_mapping,
-                          gdn_rssm_out_view persistent_cols, gdn_rssm_out_view persistent_accepted, int64_t rows,
-                          int64_t plan_capacity, int64_t spec_query_len, int64_t null_block, int32_t align,
-                          int32_t publish, void *stream) {
+static int prepare_grouped_plan(GroupedPlanParams &p, gdn_rssm_index_view sampled, const gdn_rssm_plan_group *groups,
+                                int32_t num_groups, int32_t *source, int32_t *length, int32_t *final_indices,
+                                int32_t *boundary_indices, int32_t *boundary_lengths, int32_t *valid, int32_t *col,
+                                gdn_rssm_index_view idx_mapping, gdn_rssm_out_view persistent_cols,
+                                gdn_rssm_out_view persistent_accepted, int64_t rows, int64_t plan_capacity,
+                                int64_t spec_query_len, int64_t null_block, int32_t align, int32_t publish) {
   GDN_REQUIRE(null_block == 0, "the null block id must be 0 (page zero is reserved)");
   GDN_REQUIRE(groups != nullptr && num_groups >= 1 && num_groups <= 3, "one recovery bucket supports one to three groups");
   GDN_REQUIRE(rows > 0 && rows <= plan_capacity, "grouped recovery rows out of range");
@@ -386,7 +387,7 @@ int gdn_rssm_grouped_plan(gdn_rssm_index_view sampled, const gdn_rssm_plan_group
   GDN_REQUIRE(view_ok(sampled), "sampled counts must be an int view");
   GDN_REQUIRE(source && length && final_indices && boundary_indices && boundary_lengths && valid && col,
               "plan output pointer is null");
-  GroupedPlanParams p{};
+  p = GroupedPlanParams{};
   for (int i = 0; i < num_groups; ++i) {
     const gdn_rssm_plan_group &g = groups[i];
     GDN_REQUIRE(view_ok(g.state_indices) && g.state_indices.length >= rows, "group state indices are too short");
@@ -428,6 +429,109 @@ int gdn_rssm_grouped_plan(gdn_rssm_index_view sampled, const gdn_rssm_plan_group
   p.null_block = null_block;
   p.align = align;
   p.publish = align && publish;
+  return GDN_RSSM_OK;
+}
+
+// The conv compaction's tables and geometry (not its plan arrays).
+static int prepare_conv(ConvParams &p, const int64_t *conv_addrs, const int64_t *conv_block_strides,
+                        const int64_t *conv_dim_strides, const int64_t *conv_token_strides, int64_t rows,
+                        int64_t layers, int64_t plan_capacity, int64_t conv_dim, int64_t history, int64_t window,
+                        int64_t num_blocks, int64_t null_block, int32_t elem_dtype, int32_t align) {
+  GDN_REQUIRE(null_block == 0, "the null block id must be 0 (page zero is reserved)");
+  GDN_REQUIRE(rows >= 0 && layers > 0 && plan_capacity > 0 && rows <= plan_capacity, "conv geometry");
+  GDN_REQUIRE(conv_dim > 0 && history > 0 && window >= history, "conv state is shorter than its window");
+  GDN_REQUIRE(history <= 8, "conv history longer than 8 tokens");
+  GDN_REQUIRE(conv_dim <= int64_t{65535} * 64, "conv state has too many channels");
+  GDN_REQUIRE(window <= 64, "conv state window longer than 64 tokens");
+  GDN_REQUIRE(layers * rows < (int64_t(1) << 31), "conv launch grid too large");
+  const int es = host_dtype_size(elem_dtype);
+  GDN_REQUIRE(host_dtype_is_float(elem_dtype) && (es == 2 || es == 4), "conv state must be FP32, BF16 or FP16");
+  if (rows == 0) return GDN_RSSM_OK;
+  GDN_REQUIRE(conv_addrs && conv_block_strides && conv_dim_strides && conv_token_strides, "conv table pointer is null");
+  p = ConvParams{};
+  p.addrs = conv_addrs;
+  p.block_strides = conv_block_strides;
+  p.dim_strides = conv_dim_strides;
+  p.token_strides = conv_token_strides;
+  p.rows = rows;
+  p.layers = layers;
+  p.capacity = plan_capacity;
+  p.conv_dim = conv_dim;
+  p.history = history;
+  p.window = window;
+  p.num_blocks = num_blocks;
+  p.null_block = null_block;
+  p.align = align;
+  p.elem_size = es;
+  return GDN_RSSM_OK;
+}
+
+// The plan arrays a separate fold / conv compaction reads.
+static int plan_arrays_ok(const gdn_rssm_index_view &source, const int32_t *lengths, const int32_t *final_indices,
+                          const int32_t *boundary_indices, const int32_t *boundary_lengths, int64_t plan_len) {
+  GDN_REQUIRE(lengths && final_indices && boundary_indices && boundary_lengths && plan_len > 0,
+              "plan array pointer is null");
+  GDN_REQUIRE(view_ok(source), "source indices must be an int32/int64 view");
+  return GDN_RSSM_OK;
+}
+
+#define GDN_TRY(call)              \
+  do {                             \
+    const int _rc = (call);        \
+    if (_rc != GDN_RSSM_OK) return _rc; \
+  } while (0)
+
+}  // namespace gdn_rssm
+
+extern "C" {
+
+int gdn_rssm_fold(const int64_t *state_addrs, const int64_t *state_block_strides, const int64_t *corr_addrs,
+                  const int64_t *corr_block_strides, const int64_t *key_addrs, const int64_t *key_block_strides,
+                  const int64_t *decay_addrs, const int64_t *decay_block_strides, const int32_t *layer_groups,
+                  gdn_rssm_index_view source, const int32_t *lengths, const int32_t *final_indices,
+                  const int32_t *boundary_indices, const int32_t *boundary_lengths, int64_t plan_len,
+                  const int64_t *config, int64_t config_len, int32_t state_dtype, int32_t key_dtype, int32_t key_dim,
+                  int32_t value_dim, uint32_t flags, void *stream) {
+  FoldParams p{};
+  GDN_TRY(prepare_fold(p, state_addrs, state_block_strides, corr_addrs, corr_block_strides, key_addrs,
+                       key_block_strides, decay_addrs, decay_block_strides, layer_groups, config, config_len,
+                       state_dtype, key_dtype, key_dim, value_dim, flags));
+  if (p.rows == 0) return GDN_RSSM_OK;
+  GDN_TRY(plan_arrays_ok(source, lengths, final_indices, boundary_indices, boundary_lengths, plan_len));
+  p.source = source;
+  p.lengths = lengths;
+  p.finals = final_indices;
+  p.boundaries = boundary_indices;
+  p.boundary_lens = boundary_lengths;
+  p.plan_len = plan_len;
+  const bool packed = (flags & GDN_RSSM_FOLD_PACKED) != 0;
+  return launch_fold(p, key_dim, state_dtype, packed ? GDN_RSSM_F32 : key_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int gdn_rssm_commit_plan(gdn_rssm_index_view num_accepted, gdn_rssm_index_view request_indices,
+                         gdn_rssm_index_view state_indices, gdn_rssm_index_view query_start_loc,
+                         gdn_rssm_table_view block_table, gdn_rssm_index_view num_computed, int32_t *commit_lens,
+                         int32_t *final_indices, int32_t *boundary_indices, int32_t *boundary_lengths,
+                         int32_t *align_valid, int32_t *align_col, int64_t rows, int64_t spec_query_len,
+                         int64_t num_blocks, int64_t block_size, int64_t null_block, void *stream) {
+  CommitPlanParams p{};
+  GDN_TRY(prepare_commit_plan(p, num_accepted, request_indices, state_indices, query_start_loc, block_table,
+                              num_computed, commit_lens, final_indices, boundary_indices, boundary_lengths,
+                              align_valid, align_col, rows, spec_query_len, num_blocks, block_size, null_block));
+  if (rows == 0) return GDN_RSSM_OK;
+  return launch_commit_plan(p, static_cast<cudaStream_t>(stream));
+}
+
+int gdn_rssm_grouped_plan(gdn_rssm_index_view sampled, const gdn_rssm_plan_group *groups, int32_t num_groups,
+                          int32_t *source, int32_t *length, int32_t *final_indices, int32_t *boundary_indices,
+                          int32_t *boundary_lengths, int32_t *valid, int32_t *col, gdn_rssm_index_view idx_mapping,
+                          gdn_rssm_out_view persistent_cols, gdn_rssm_out_view persistent_accepted, int64_t rows,
+                          int64_t plan_capacity, int64_t spec_query_len, int64_t null_block, int32_t align,
+                          int32_t publish, void *stream) {
+  GroupedPlanParams p{};
+  GDN_TRY(prepare_grouped_plan(p, sampled, groups, num_groups, source, length, final_indices, boundary_indices,
+                               boundary_lengths, valid, col, idx_mapping, persistent_cols, persistent_accepted, rows,
+                               plan_capacity, spec_query_len, null_block, align, publish));
   return launch_grouped_plan(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -460,25 +564,12 @@ int gdn_rssm_compact_conv(const int64_t *conv_addrs, const int64_t *conv_block_s
                           const int32_t *boundary_lengths, int64_t plan_len, int64_t rows, int64_t layers,
                           int64_t plan_capacity, int64_t conv_dim, int64_t history, int64_t window,
                           int64_t num_blocks, int64_t null_block, int32_t elem_dtype, int32_t align, void *stream) {
-  GDN_REQUIRE(null_block == 0, "the null block id must be 0 (page zero is reserved)");
-  GDN_REQUIRE(rows >= 0 && layers > 0 && plan_capacity > 0 && rows <= plan_capacity, "conv geometry");
-  GDN_REQUIRE(conv_dim > 0 && history > 0 && window >= history, "conv state is shorter than its window");
-  GDN_REQUIRE(history <= 8, "conv history longer than 8 tokens");
-  GDN_REQUIRE(conv_dim <= int64_t{65535} * 64, "conv state has too many channels");
-  GDN_REQUIRE(window <= 64, "conv state window longer than 64 tokens");
-  GDN_REQUIRE(layers * rows < (int64_t(1) << 31), "conv launch grid too large");
-  if (rows == 0) return GDN_RSSM_OK;
-  GDN_REQUIRE(conv_addrs && conv_block_strides && conv_dim_strides && conv_token_strides && layer_groups && lengths &&
-                  final_indices && boundary_indices && boundary_lengths && plan_len > 0,
-              "conv table pointer is null");
-  GDN_REQUIRE(view_ok(source), "conv source indices must be an int view");
-  const int es = host_dtype_size(elem_dtype);
-  GDN_REQUIRE(host_dtype_is_float(elem_dtype) && (es == 2 || es == 4), "conv state must be FP32, BF16 or FP16");
   ConvParams p{};
-  p.addrs = conv_addrs;
-  p.block_strides = conv_block_strides;
-  p.dim_strides = conv_dim_strides;
-  p.token_strides = conv_token_strides;
+  GDN_TRY(prepare_conv(p, conv_addrs, conv_block_strides, conv_dim_strides, conv_token_strides, rows, layers,
+                       plan_capacity, conv_dim, history, window, num_blocks, null_block, elem_dtype, align));
+  if (rows == 0) return GDN_RSSM_OK;
+  GDN_REQUIRE(layer_groups != nullptr, "conv table pointer is null");
+  GDN_TRY(plan_arrays_ok(source, lengths, final_indices, boundary_indices, boundary_lengths, plan_len));
   p.layer_groups = layer_groups;
   p.source = source;
   p.lengths = lengths;
@@ -486,16 +577,7 @@ int gdn_rssm_compact_conv(const int64_t *conv_addrs, const int64_t *conv_block_s
   p.boundaries = boundary_indices;
   p.boundary_lens = boundary_lengths;
   p.plan_len = plan_len;
-  p.rows = rows;
-  p.layers = layers;
-  p.capacity = plan_capacity;
-  p.conv_dim = conv_dim;
-  p.history = history;
-  p.window = window;
-  p.num_blocks = num_blocks;
-  p.null_block = null_block;
-  p.align = align;
-  return launch_compact_conv(p, es, static_cast<cudaStream_t>(stream));
+  return launch_compact_conv(p, p.elem_size, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

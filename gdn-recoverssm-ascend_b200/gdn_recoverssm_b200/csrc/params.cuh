@@ -54,8 +54,9 @@ struct ConvParams {
   const int32_t *lengths, *finals, *boundaries, *boundary_lens;
   int64_t plan_len, rows, layers, capacity, conv_dim, history, window, num_blocks, null_block;
   int32_t align;
-  int32_t chunk;  // channels per CTA (blockIdx.y)
-  int32_t vec;    // 1: stage whole chunks through shared memory with 16-byte copies
+  int32_t chunk;      // channels per CTA (blockIdx.y)
+  int32_t vec;        // 1: stage whole chunks through shared memory with 16-byte copies
+  int32_t elem_size;  // bytes per conv element (2 or 4)
 };
 
 }  // namespace gdn_rssm

@@ -39,14 +39,16 @@ __device__ __forceinline__ int32_t mul_wrap32(int32_t a, int32_t b) {
   return static_cast<int32_t>(static_cast<uint32_t>(a) * static_cast<uint32_t>(b));
 }
 
-__global__ void commit_plan_kernel(const CommitPlanParams p) {
-  // launched as a programmatic dependent of the kernel before it (the sampler
-  // in serving, verify in a bench step): wait for it before reading its
-  // results, then let the fold start launching (it waits for this grid)
-  ptx::wait_prerequisite_grid();
-  ptx::launch_dependents();
-  const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (r >= p.rows) return;
+// One plan row: what the conv compaction and the fold of that row do, in the
+// form the plan arrays store it (invalid rows: length 0, null pages).
+struct RowPlan {
+  int64_t source;  // the page folded from (grouped plans store it masked)
+  int64_t request;
+  int32_t length, final_page, boundary, boundary_len, valid, col;
+};
+
+// Per-context plan of row r (_prepare_commit_plan_kernel, kernels.py:936-1072).
+__device__ __forceinline__ RowPlan context_row_plan(const CommitPlanParams &p, int64_t r) {
   const int64_t nul = p.null_block;
   const int64_t source = load_index(p.state, r);
   const int64_t req = p.request.data ? load_index(p.request, r) : r;
@@ -83,73 +85,117 @@ __global__ void commit_plan_kernel(const CommitPlanParams p) {
     valid = valid && c >= 0;
     if (!(boundary > nul && boundary < p.num_blocks)) blen = 0;
   }
-  p.lens[r] = valid ? n : 0;
-  p.finals[r] = static_cast<int32_t>(valid ? fin : nul);
-  p.boundaries[r] = static_cast<int32_t>(valid ? boundary : nul);
-  p.boundary_lens[r] = valid ? blen : 0;
-  p.valid[r] = valid ? 1 : 0;
-  p.col[r] = colv;
+  RowPlan out;
+  out.source = source;
+  out.request = req;
+  out.length = valid ? n : 0;
+  out.final_page = static_cast<int32_t>(valid ? fin : nul);
+  out.boundary = static_cast<int32_t>(valid ? boundary : nul);
+  out.boundary_len = valid ? blen : 0;
+  out.valid = valid ? 1 : 0;
+  out.col = colv;
+  return out;
 }
 
+__device__ __forceinline__ void store_context_plan(const CommitPlanParams &p, int64_t r, const RowPlan &pl) {
+  p.lens[r] = pl.length;
+  p.finals[r] = pl.final_page;
+  p.boundaries[r] = pl.boundary;
+  p.boundary_lens[r] = pl.boundary_len;
+  p.valid[r] = pl.valid;
+  p.col[r] = pl.col;
+}
 
-__global__ void grouped_plan_kernel(const GroupedPlanParams p) {
-  ptx::wait_prerequisite_grid();  // as in commit_plan_kernel
+__global__ void commit_plan_kernel(const CommitPlanParams p) {
+  // launched as a programmatic dependent of the kernel before it (the sampler
+  // in serving, verify in a bench step): wait for it before reading its
+  // results, then let the fold start launching (it waits for this grid)
+  ptx::wait_prerequisite_grid();
   ptx::launch_dependents();
-  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (row >= p.rows) return;
+  const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (r >= p.rows) return;
+  store_context_plan(p, r, context_row_plan(p, r));
+}
+
+// Grouped plan of (group gi, row) (_grouped_plan_kernel, grouped_commit.py:31-222):
+// the source is stored masked, and a group-local invalid boundary becomes
+// null before the bucket-wide pool bound of the fold could make it valid.
+__device__ __forceinline__ RowPlan group_row_plan(const GroupedPlanParams &p, int gi, int64_t row) {
   const int64_t nul = p.null_block;
+  const gdn_rssm_plan_group &g = p.groups[gi];
+  const int64_t req = load_index(g.request_indices, row);
+  const int64_t source = load_index(g.state_indices, row);
+  const int64_t bos = load_index(g.query_start_loc, row), eos = load_index(g.query_start_loc, row + 1);
+  const int64_t qlen = eos - bos;
+  bool row_ok = true;
+  const int64_t acc = static_cast<int32_t>(load_index_checked(p.sampled, req, row_ok));
+  int64_t n = acc > 0 ? acc : 0;
+  n = n < qlen ? n : qlen;
+  n = n < p.Q ? n : p.Q;
+  int64_t fin = source, boundary = nul, blen = 0, colv = 0;
+  bool computed_ok = true;
+  if (p.align) {
+    const int64_t c = load_index_checked(g.num_computed, req, row_ok);
+    if (req < 0 || req >= g.block_table.rows) row_ok = false;
+    computed_ok = c >= 0;
+    const int64_t B = g.block_size, W = g.block_table.cols;
+    const int64_t pos = c + n;
+    colv = floordiv(pos - 1 > 0 ? pos - 1 : 0, B);
+    colv = colv < W - 1 ? colv : W - 1;
+    fin = row_ok ? load_table(g.block_table, req, colv) : nul;
+    const int64_t nxt = (floordiv(c, B) + 1) * B;
+    const bool crossed = pos >= nxt;
+    blen = static_cast<int32_t>(nxt - c);
+    const int64_t bcol = floordiv(nxt, B) - 1;
+    boundary = (row_ok && crossed && computed_ok && bcol >= 0 && bcol < W) ? load_table(g.block_table, req, bcol) : nul;
+  }
+  const bool geometry = bos >= 0 && bos <= eos && qlen <= p.Q;
+  const bool valid = row_ok && geometry && source > nul && source < g.num_blocks && fin > nul && fin < g.num_blocks &&
+                     n > 0 && n <= qlen && computed_ok;
+  if (!(boundary > nul && boundary < g.num_blocks)) {
+    blen = 0;
+    boundary = nul;
+  }
+  RowPlan out;
+  out.source = valid ? source : nul;
+  out.request = req;
+  out.length = valid ? static_cast<int32_t>(n) : 0;
+  out.final_page = static_cast<int32_t>(valid ? fin : nul);
+  out.boundary = static_cast<int32_t>(valid ? boundary : nul);
+  out.boundary_len = valid ? static_cast<int32_t>(blen) : 0;
+  out.valid = valid ? 1 : 0;
+  out.col = static_cast<int32_t>(colv);
+  return out;
+}
+
+__device__ __forceinline__ void store_group_plan(const GroupedPlanParams &p, int gi, int64_t row, const RowPlan &pl) {
+  const int64_t off = gi * p.capacity + row;
+  p.source[off] = static_cast<int32_t>(pl.source);
+  p.length[off] = pl.length;
+  p.finals[off] = pl.final_page;
+  p.boundaries[off] = pl.boundary;
+  p.boundary_lens[off] = pl.boundary_len;
+  p.valid[off] = pl.valid;
+  p.col[off] = pl.col;
+}
+
+// Every group's plan of one row, stored, then (align + publish) the row's
+// publication: when all groups are valid and agree on column and request,
+// persistent_cols[slot] = col and persistent_accepted[slot] = 1 with
+// slot = idx_mapping[request] (grouped_commit.py:214-222).
+__device__ __forceinline__ void grouped_plan_row(const GroupedPlanParams &p, int64_t row) {
   bool all_valid = true;
   int64_t shared_col = -1, shared_req = -1;
   for (int gi = 0; gi < p.num_groups; ++gi) {
-    const gdn_rssm_plan_group &g = p.groups[gi];
-    const int64_t req = load_index(g.request_indices, row);
-    const int64_t source = load_index(g.state_indices, row);
-    const int64_t bos = load_index(g.query_start_loc, row), eos = load_index(g.query_start_loc, row + 1);
-    const int64_t qlen = eos - bos;
-    bool row_ok = true;
-    const int64_t acc = static_cast<int32_t>(load_index_checked(p.sampled, req, row_ok));
-    int64_t n = acc > 0 ? acc : 0;
-    n = n < qlen ? n : qlen;
-    n = n < p.Q ? n : p.Q;
-    int64_t fin = source, boundary = nul, blen = 0, colv = 0;
-    bool computed_ok = true;
-    if (p.align) {
-      const int64_t c = load_index_checked(g.num_computed, req, row_ok);
-      if (req < 0 || req >= g.block_table.rows) row_ok = false;
-      computed_ok = c >= 0;
-      const int64_t B = g.block_size, W = g.block_table.cols;
-      const int64_t pos = c + n;
-      colv = floordiv(pos - 1 > 0 ? pos - 1 : 0, B);
-      colv = colv < W - 1 ? colv : W - 1;
-      fin = row_ok ? load_table(g.block_table, req, colv) : nul;
-      const int64_t nxt = (floordiv(c, B) + 1) * B;
-      const bool crossed = pos >= nxt;
-      blen = static_cast<int32_t>(nxt - c);
-      const int64_t bcol = floordiv(nxt, B) - 1;
-      boundary = (row_ok && crossed && computed_ok && bcol >= 0 && bcol < W) ? load_table(g.block_table, req, bcol) : nul;
-    }
-    const bool geometry = bos >= 0 && bos <= eos && qlen <= p.Q;
-    bool valid = row_ok && geometry && source > nul && source < g.num_blocks && fin > nul && fin < g.num_blocks &&
-                 n > 0 && n <= qlen && computed_ok;
-    if (!(boundary > nul && boundary < g.num_blocks)) {
-      blen = 0;
-      boundary = nul;
-    }
-    const int64_t off = gi * p.capacity + row;
-    p.source[off] = static_cast<int32_t>(valid ? source : nul);
-    p.length[off] = valid ? static_cast<int32_t>(n) : 0;
-    p.finals[off] = static_cast<int32_t>(valid ? fin : nul);
-    p.boundaries[off] = static_cast<int32_t>(valid ? boundary : nul);
-    p.boundary_lens[off] = valid ? static_cast<int32_t>(blen) : 0;
-    p.valid[off] = valid ? 1 : 0;
-    p.col[off] = static_cast<int32_t>(colv);
+    const RowPlan pl = group_row_plan(p, gi, row);
+    store_group_plan(p, gi, row, pl);
     if (gi == 0) {
-      shared_col = colv;
-      shared_req = req;
+      shared_col = pl.col;
+      shared_req = pl.request;
     } else {
-      all_valid = all_valid && colv == shared_col && req == shared_req;
+      all_valid = all_valid && pl.col == shared_col && pl.request == shared_req;
     }
-    all_valid = all_valid && valid;
+    all_valid = all_valid && pl.valid;
   }
   if (p.align && p.publish) {
     bool ok = true;
@@ -159,6 +205,14 @@ __global__ void grouped_plan_kernel(const GroupedPlanParams p) {
       store_index(p.accepted_out, slot, 1);
     }
   }
+}
+
+__global__ void grouped_plan_kernel(const GroupedPlanParams p) {
+  ptx::wait_prerequisite_grid();  // as in commit_plan_kernel
+  ptx::launch_dependents();
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (row >= p.rows) return;
+  grouped_plan_row(p, row);
 }
 
 

@@ -194,13 +194,20 @@ void verify(const Tensor &q, const Tensor &k, const Tensor &v, const Tensor &g, 
   verify_ext(q, k, v, g, beta, state, correction, key, decay, out, qsl, indices, config, scale, 0);
 }
 
-void fold_ext(const Tensor &state, const Tensor &correction, const Tensor &key, const Tensor &decay,
-              const Tensor &state_addrs, const Tensor &state_block_strides, const Tensor &corr_addrs,
-              const Tensor &corr_block_strides, const Tensor &key_addrs, const Tensor &key_block_strides,
-              const Tensor &decay_addrs, const Tensor &decay_block_strides, const Tensor &layer_groups,
-              const Tensor &source, const Tensor &lengths, const Tensor &final_indices,
-              const Tensor &boundary_indices, const Tensor &boundary_lengths, at::IntArrayRef config,
-              int64_t flags) {
+// Checks of the fold's tensors and configuration (everything but the plan
+// arrays), shared by fold_ext and the fused commits.
+struct FoldTables {
+  const int64_t *state_addrs, *state_bs, *corr_addrs, *corr_bs, *key_addrs, *key_bs, *decay_addrs, *decay_bs;
+  const int32_t *layer_groups;
+  int32_t state_code, key_code, K, V;
+};
+
+FoldTables check_fold_tensors(const Tensor &state, const Tensor &correction, const Tensor &key, const Tensor &decay,
+                              const Tensor &state_addrs, const Tensor &state_block_strides, const Tensor &corr_addrs,
+                              const Tensor &corr_block_strides, const Tensor &key_addrs,
+                              const Tensor &key_block_strides, const Tensor &decay_addrs,
+                              const Tensor &decay_block_strides, const Tensor &layer_groups, at::IntArrayRef config,
+                              int64_t flags) {
   TORCH_CHECK(config.size() == GDN_RSSM_FOLD_FIELDS, "GDN RecoverSSM: fold config must have 17 fields");
   TORCH_CHECK(state.is_cuda(), "GDN RecoverSSM: fold requires CUDA tensors");
   const int64_t layers = config[1];
@@ -217,9 +224,6 @@ void fold_ext(const Tensor &state, const Tensor &correction, const Tensor &key, 
     check_table(decay_block_strides, state, layers, at::kLong, "decay_block_strides");
   }
   check_table(layer_groups, state, layers, at::kInt, "layer_groups");
-  const int64_t plan = lengths.numel();
-  TORCH_CHECK(config[7] > 0 && plan % config[7] == 0 && plan / config[7] > 0, "GDN RecoverSSM: invalid plan tensor");
-  for (auto *t : {&lengths, &final_indices, &boundary_indices, &boundary_lengths}) check_plan_out(*t, state, plan, "plan");
   TORCH_CHECK(state.dim() == 4 && state.stride(3) == 1 && state.size(1) == config[2] && config[9] == state.stride(1) &&
                   config[10] == state.stride(2),
               "GDN RecoverSSM: fold config does not match the state geometry");
@@ -244,20 +248,46 @@ void fold_ext(const Tensor &state, const Tensor &correction, const Tensor &key, 
     TORCH_CHECK(config[6] <= key.size(0) && config[6] <= decay.size(0),
                 "GDN RecoverSSM: fold record rows exceed the key / decay records");
   }
+  auto ptr64 = [](const Tensor &t) { return t.defined() && t.numel() ? t.data_ptr<int64_t>() : nullptr; };
+  FoldTables f{};
+  f.state_addrs = state_addrs.data_ptr<int64_t>();
+  f.state_bs = state_block_strides.data_ptr<int64_t>();
+  f.corr_addrs = corr_addrs.data_ptr<int64_t>();
+  f.corr_bs = corr_block_strides.data_ptr<int64_t>();
+  f.key_addrs = packed ? nullptr : ptr64(key_addrs);
+  f.key_bs = packed ? nullptr : ptr64(key_block_strides);
+  f.decay_addrs = packed ? nullptr : ptr64(decay_addrs);
+  f.decay_bs = packed ? nullptr : ptr64(decay_block_strides);
+  f.layer_groups = layer_groups.data_ptr<int32_t>();
+  f.state_code = code_of(state.scalar_type());
+  f.key_code = packed ? GDN_RSSM_F32 : code_of(key.scalar_type());
+  f.K = static_cast<int32_t>(K);
+  f.V = static_cast<int32_t>(V);
+  return f;
+}
+
+void fold_ext(const Tensor &state, const Tensor &correction, const Tensor &key, const Tensor &decay,
+              const Tensor &state_addrs, const Tensor &state_block_strides, const Tensor &corr_addrs,
+              const Tensor &corr_block_strides, const Tensor &key_addrs, const Tensor &key_block_strides,
+              const Tensor &decay_addrs, const Tensor &decay_block_strides, const Tensor &layer_groups,
+              const Tensor &source, const Tensor &lengths, const Tensor &final_indices,
+              const Tensor &boundary_indices, const Tensor &boundary_lengths, at::IntArrayRef config,
+              int64_t flags) {
+  const FoldTables f = check_fold_tensors(state, correction, key, decay, state_addrs, state_block_strides, corr_addrs,
+                                          corr_block_strides, key_addrs, key_block_strides, decay_addrs,
+                                          decay_block_strides, layer_groups, config, flags);
+  const int64_t plan = lengths.numel();
+  TORCH_CHECK(config[7] > 0 && plan % config[7] == 0 && plan / config[7] > 0, "GDN RecoverSSM: invalid plan tensor");
+  for (auto *t : {&lengths, &final_indices, &boundary_indices, &boundary_lengths}) check_plan_out(*t, state, plan, "plan");
   auto src = index_view(source, state, "source");
   const c10::cuda::CUDAGuard guard(state.device());
   const auto stream = at::cuda::getCurrentCUDAStream(state.get_device()).stream();
   std::vector<int64_t> cfg(config.begin(), config.end());
-  auto ptr64 = [](const Tensor &t) { return t.defined() && t.numel() ? t.data_ptr<int64_t>() : nullptr; };
-  check_rc(gdn_rssm_fold(state_addrs.data_ptr<int64_t>(), state_block_strides.data_ptr<int64_t>(),
-                         corr_addrs.data_ptr<int64_t>(), corr_block_strides.data_ptr<int64_t>(),
-                         packed ? nullptr : ptr64(key_addrs), packed ? nullptr : ptr64(key_block_strides),
-                         packed ? nullptr : ptr64(decay_addrs), packed ? nullptr : ptr64(decay_block_strides),
-                         layer_groups.data_ptr<int32_t>(), src, lengths.data_ptr<int32_t>(),
-                         final_indices.data_ptr<int32_t>(), boundary_indices.data_ptr<int32_t>(),
-                         boundary_lengths.data_ptr<int32_t>(), plan, cfg.data(), static_cast<int64_t>(cfg.size()),
-                         code_of(state.scalar_type()), packed ? GDN_RSSM_F32 : code_of(key.scalar_type()),
-                         static_cast<int32_t>(K), static_cast<int32_t>(V), static_cast<uint32_t>(flags), stream));
+  check_rc(gdn_rssm_fold(f.state_addrs, f.state_bs, f.corr_addrs, f.corr_bs, f.key_addrs, f.key_bs, f.decay_addrs,
+                         f.decay_bs, f.layer_groups, src, lengths.data_ptr<int32_t>(), final_indices.data_ptr<int32_t>(),
+                         boundary_indices.data_ptr<int32_t>(), boundary_lengths.data_ptr<int32_t>(), plan, cfg.data(),
+                         static_cast<int64_t>(cfg.size()), f.state_code, f.key_code, f.K, f.V,
+                         static_cast<uint32_t>(flags), stream));
 }
 
 void fold(const Tensor &state, const Tensor &correction, const Tensor &key, const Tensor &decay,

@@ -47,26 +47,39 @@ int launch_verify_kernel(VerifyLaunch &L) {
   int rc = encode_state_map(&map, L.state, L.state_dtype, DIM, TC ? DIM : 32, L.p.value_heads, L.p.blocks,
                             L.state_bs, L.state_hs, L.state_vs);
   if (rc != GDN_RSSM_OK) return rc;
-  constexpr int smem = TC ? verify_tc_smem_bytes<QT, Act>() : verify_smem_bytes<DIM, QT, Act, St>();
-  // the tensor-core kernel has a separate instantiation for the fused gating
-  // prologue, so the plain form keeps its register budget
+  // the tensor-core kernel has separate instantiations for the fused gating
+  // prologue (so the plain form keeps its register budget) and for exact
+  // operands: bf16 / fp16 q, k used as given are exact tf32 values
   const int gated = (L.p.flags & kGateInKernel) ? 1 : 0;
+  constexpr bool low_precision = !std::is_same<Act, float>::value;
+  const int exact = (TC && low_precision && !(L.p.flags & GDN_RSSM_NORMALIZE_QK)) ? 1 : 0;
   void (*kernel)(const CUtensorMap, const VerifyParams) = nullptr;
+  int smem = 0;
   if constexpr (TC) {
-    kernel = gated ? verify_tc_kernel<QT, Act, true> : verify_tc_kernel<QT, Act, false>;
+    if constexpr (low_precision) {
+      if (exact) {
+        kernel = gated ? verify_tc_kernel<QT, Act, true, true> : verify_tc_kernel<QT, Act, false, true>;
+        smem = verify_tc_smem_bytes<QT, Act, true>();
+      }
+    }
+    if (!exact) {
+      kernel = gated ? verify_tc_kernel<QT, Act, true, false> : verify_tc_kernel<QT, Act, false, false>;
+      smem = verify_tc_smem_bytes<QT, Act, false>();
+    }
   } else {
     kernel = verify_kernel<DIM, QT, Act, St>;
+    smem = verify_smem_bytes<DIM, QT, Act, St>();
   }
-  static bool configured[2][64] = {};
+  static bool configured[2][2][64] = {};
   int dev = 0;
   GDN_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) {
     set_error("GDN RecoverSSM: device ordinal out of range");
     return GDN_RSSM_EUNSUPPORTED;
   }
-  if (!configured[gated][dev]) {
+  if (!configured[gated][exact][dev]) {
     GDN_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured[gated][dev] = true;
+    configured[gated][exact][dev] = true;
   }
   const int64_t units = L.p.rows * L.p.value_heads;
   if (units <= 0) return GDN_RSSM_OK;

@@ -44,15 +44,21 @@
 // word; tensor memory is released on every path after it was allocated.
 #pragma once
 
+#include <type_traits>
+
 #include "verify.cuh"
 
 namespace gdn_rssm {
 
-template <int QT, typename Act>
+// EXACT: the window's vectors are exact tf32 values (bf16 / fp16 inputs used as
+// they are, no in-kernel normalisation, q unscaled), so lo(X) = 0 and the
+// pass-1 operand holds X alone; the output is scaled after the dot products.
+template <int QT, typename Act, bool EXACT>
 struct VerifyTcShape {
   static constexpr int DIM = 128;
   static constexpr int NJ = 2 * QT;                    // dot products per state row
-  static constexpr int NB = (2 * NJ + 15) / 16 * 16;   // pass-1 B rows: hi(X), lo(X), zero padding
+  static constexpr int XROWS = EXACT ? NJ : 2 * NJ;    // pass-1 B rows with data: X, or hi(X) and lo(X)
+  static constexpr int NB = (XROWS + 15) / 16 * 16;    // ... padded with zero rows to the MMA's N
   static constexpr int TMEM_COLS = 128;
   static constexpr uint32_t D_COL = 0;                 // pass-1 accumulator: NB columns
   static constexpr uint32_t D2_COL = 32;               // pass-2 accumulator: 16 columns
@@ -92,6 +98,7 @@ struct VerifyTcShape {
   // the 128-byte swizzle atoms require
   static constexpr int SMEM = TILE + B2_BYTES + B_BYTES + X32_BYTES + static_cast<int>(sizeof(Small));
   static_assert(NB <= static_cast<int>(D2_COL) && (NB == 16 || NB == 32), "accumulator columns");
+  static_assert(!EXACT || !std::is_same<Act, float>::value, "fp32 activations are not exact tf32 values");
   static_assert(NJ <= NB2, "pass-2 operand rows");
   static_assert(!GRAM_ALL || QT * QT * 4 == kVerifyThreads, "gram_all_warps: four threads per Gram pair");
   static_assert(B_SLAB % 1024 == 0 && B2_SLAB % 1024 == 0, "operand slabs must stay 1024-byte aligned");
@@ -108,11 +115,12 @@ constexpr int verify_tc_min_blocks() {
 constexpr int kSmemPerSm = 233472;
 constexpr int kSmemReservedPerCta = 1024;
 
-template <int QT, typename Act>
+template <int QT, typename Act, bool EXACT>
 constexpr int verify_tc_smem_bytes() {
-  static_assert(verify_tc_min_blocks<QT>() * (VerifyTcShape<QT, Act>::SMEM + kSmemReservedPerCta) <= kSmemPerSm,
+  static_assert(verify_tc_min_blocks<QT>() * (VerifyTcShape<QT, Act, EXACT>::SMEM + kSmemReservedPerCta) <=
+                    kSmemPerSm,
                 "the verify CTAs of one SM must fit its shared memory");
-  return VerifyTcShape<QT, Act>::SMEM;
+  return VerifyTcShape<QT, Act, EXACT>::SMEM;
 }
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
@@ -127,7 +135,7 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 // the order: k_s . k_t for t = 1..Q-1, s < t, then k_s . q_t for t = 0..Q-1,
 // s <= t.  A reduce-scatter over the warp leaves each pair's slab sum on known
 // lanes, which store part[g][pair].
-template <int QT, int NJ, int B_SLAB>
+template <int QT, int NJ, int B_SLAB, bool EXACT>
 __device__ __forceinline__ void gram_partials(const unsigned char *bop, float (*part)[QT * QT], int g, int lane) {
   constexpr int NP = QT * QT;
   const unsigned char *slab = bop + g * B_SLAB;
@@ -135,10 +143,13 @@ __device__ __forceinline__ void gram_partials(const unsigned char *bop, float (*
   float x[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
-    const int jl = NJ + j;
     const float hi = *reinterpret_cast<const float *>(slab + j * 128 + ((chunk ^ (j & 7)) << 4) + word);
-    const float lo = *reinterpret_cast<const float *>(slab + jl * 128 + ((chunk ^ (jl & 7)) << 4) + word);
-    x[j] = hi + lo;
+    if constexpr (EXACT) {
+      x[j] = hi;
+    } else {
+      const int jl = NJ + j;
+      x[j] = hi + *reinterpret_cast<const float *>(slab + jl * 128 + ((chunk ^ (jl & 7)) << 4) + word);
+    }
   }
   float acc[NP];
   int p = 0;
@@ -267,11 +278,13 @@ __device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int
 }
 
 // GATED: the fused gating prologue (raw a, b in the g / beta slots).
-template <int QT, typename Act, bool GATED>
+// EXACT: see VerifyTcShape (bf16 / fp16 activations without in-kernel
+// normalisation).
+template <int QT, typename Act, bool GATED, bool EXACT>
 __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     verify_tc_kernel(const __grid_constant__ CUtensorMap state_map, const VerifyParams p) {
   ptx::launch_dependents();  // a commit plan behind it may launch; it waits for this grid
-  using Sh = VerifyTcShape<QT, Act>;
+  using Sh = VerifyTcShape<QT, Act, EXACT>;
   using Small = typename Sh::Small;
   using Window = typename Sh::Window;
   constexpr int DIM = Sh::DIM, NJ = Sh::NJ, NB = Sh::NB, EPL = DIM / 32;
@@ -408,6 +421,25 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     ptx::tmem_alloc(&sm.tmem, Sh::TMEM_COLS);
     ptx::tmem_relinquish();
   }
+  // operand rows no unit writes: the zero padding of the pass-1 operand up to
+  // the MMA's N, and the rows of the last pass-2 data group past the window
+  // (they reach accumulator columns that are never read; zeroed once here)
+  if constexpr (NB > Sh::XROWS) {
+    constexpr int PAD = (NB - Sh::XROWS) * 8;  // 16-byte chunks per slab
+    for (int e = tid; e < 4 * PAD; e += kVerifyThreads) {
+      const int mm = e / PAD, rem = e % PAD;
+      *reinterpret_cast<uint4 *>(bop + mm * Sh::B_SLAB + (Sh::XROWS + rem / 8) * 128 + ((rem % 8) << 4)) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  if constexpr (8 * Sh::G2 > NJ) {
+    constexpr int PAD = (8 * Sh::G2 - NJ) * 8;
+    for (int e = tid; e < 2 * PAD; e += kVerifyThreads) {
+      const int m = e / PAD, rem = e % PAD;
+      *reinterpret_cast<uint4 *>(b2op + m * Sh::B2_SLAB + (NJ + rem / 8) * 128 + ((rem % 8) << 4)) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
   const int gpair = Sh::GRAM_ALL ? gram_pair_rows<QT>(tid >> 2) : 0;  // this thread's Gram pair (Q = 8)
   Inputs ic;
   load_inputs(ic, c0, m0);
@@ -468,14 +500,6 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       if constexpr (!GATED) {
         if (tid < QT) stage_gates(0.f, 0.f);
       }
-      if constexpr (NB > 2 * NJ) {  // zero padding rows of B (Q < 4)
-        constexpr int PAD = (NB - 2 * NJ) * 8;  // 16-byte chunks per slab
-        for (int e = tid; e < 4 * PAD; e += kVerifyThreads) {
-          const int mm = e / PAD, rem = e % PAD;
-          *reinterpret_cast<uint4 *>(bop + mm * Sh::B_SLAB + (2 * NJ + rem / 8) * 128 + ((rem % 8) << 4)) =
-              make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
       float xs[PER_WARP][EPL];  // this warp's staged vectors, kept for the pass-2 operand
 #pragma unroll
       for (int c = 0; c < PER_WARP; ++c) {
@@ -504,23 +528,29 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
             for (int e = 0; e < EPL; ++e)
               store_key(p.key, row * p.key_rs + kh * p.key_hs + t * p.key_ts + lane * EPL + e, x[e], kd);
           }
-        } else {
+        } else if constexpr (!EXACT) {  // exact operands keep q unscaled: the output is scaled instead
 #pragma unroll
           for (int e = 0; e < EPL; ++e) x[e] *= p.scale;
         }
         if constexpr (Sh::GRAM_ALL)
           *reinterpret_cast<float4 *>(x32 + j * DIM + lane * EPL) = make_float4(x[0], x[1], x[2], x[3]);
-        float hi[EPL], lo[EPL];
+        const int mm = lane >> 3, ch = lane & 7;
+        if constexpr (EXACT) {
+          *reinterpret_cast<float4 *>(bop + mm * Sh::B_SLAB + j * 128 + ((ch ^ (j & 7)) << 4)) =
+              make_float4(x[0], x[1], x[2], x[3]);
+        } else {
+          float hi[EPL], lo[EPL];
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-          hi[e] = tf32_hi(x[e]);
-          lo[e] = x[e] - hi[e];
+          for (int e = 0; e < EPL; ++e) {
+            hi[e] = tf32_hi(x[e]);
+            lo[e] = x[e] - hi[e];
+          }
+          const int jl = NJ + j;
+          *reinterpret_cast<float4 *>(bop + mm * Sh::B_SLAB + j * 128 + ((ch ^ (j & 7)) << 4)) =
+              make_float4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<float4 *>(bop + mm * Sh::B_SLAB + jl * 128 + ((ch ^ (jl & 7)) << 4)) =
+              make_float4(lo[0], lo[1], lo[2], lo[3]);
         }
-        const int mm = lane >> 3, ch = lane & 7, jl = NJ + j;
-        *reinterpret_cast<float4 *>(bop + mm * Sh::B_SLAB + j * 128 + ((ch ^ (j & 7)) << 4)) =
-            make_float4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<float4 *>(bop + mm * Sh::B_SLAB + jl * 128 + ((ch ^ (jl & 7)) << 4)) =
-            make_float4(lo[0], lo[1], lo[2], lo[3]);
       }
       ptx::fence_proxy_async_smem();  // B operand -> tensor-core reads
       // ---- B, dec, beta staged by every thread; the tile has landed ---------- //
@@ -583,19 +613,11 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         *reinterpret_cast<uint2 *>(b2op + m * Sh::B2_SLAB + j * 128 + ((ch ^ (j & 7)) << 4) + (lane & 1) * 8) =
             make_uint2(*reinterpret_cast<const uint32_t *>(&b01), *reinterpret_cast<const uint32_t *>(&b23));
       }
-      if constexpr (8 * Sh::G2 > NJ) {  // zero the unused rows of the last data group
-        constexpr int PAD = (8 * Sh::G2 - NJ) * 8;  // 16-byte chunks per slab
-        for (int e = tid; e < 2 * PAD; e += kVerifyThreads) {
-          const int m = e / PAD, rem = e % PAD;
-          *reinterpret_cast<uint4 *>(b2op + m * Sh::B2_SLAB + (NJ + rem / 8) * 128 + ((rem % 8) << 4)) =
-              make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
       // ---- ... the Gram partial sums and the next units' loads ---------------- //
       if constexpr (Sh::GRAM_ALL) {
         gram_all_warps<QT>(x32, sm.gpart, gpair, tid);
       } else {
-        if (warp >= 4) gram_partials<QT, NJ, Sh::B_SLAB>(bop, sm.gpart, warp - 4, lane);
+        if (warp >= 4) gram_partials<QT, NJ, Sh::B_SLAB, EXACT>(bop, sm.gpart, warp - 4, lane);
       }
       prefetch();
       ptx::fence_proxy_async_smem();  // pass-2 operand -> tensor-core reads
@@ -649,16 +671,17 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       for (int t = 0; t < QT; ++t) {
         cr[t] = 0.f;
         if (!((vmask >> t) & 1)) continue;
-        float kv = w.A[t] * ((d[t] + d[NJ + t]) + d2[t]);
+        float kv = w.A[t] * (EXACT ? d[t] + d2[t] : (d[t] + d[NJ + t]) + d2[t]);
 #pragma unroll
         for (int s2 = 0; s2 < t; ++s2) kv = fmaf(w.mkk[t][s2], cr[s2], kv);
         cr[t] = w.beta[t] * (to_f32<Act>(ic.v[t]) - kv);
         if (writer_corr) {
           if (rec_ok) p.corr[row * p.corr_rs + hv * p.corr_hs + t * p.corr_ts + r] = cr[t];
         } else {
-          float o = w.A[t] * ((d[QT + t] + d[NJ + QT + t]) + d2[QT + t]);
+          float o = w.A[t] * (EXACT ? d[QT + t] + d2[QT + t] : (d[QT + t] + d[NJ + QT + t]) + d2[QT + t]);
 #pragma unroll
           for (int s2 = 0; s2 <= t; ++s2) o = fmaf(w.mkq[t][s2], cr[s2], o);
+          if constexpr (EXACT) o *= p.scale;
           out[(static_cast<int64_t>(m0.bos) + t) * p.out_ts + hv * DIM + r] = from_f32<Act>(o);
         }
       }

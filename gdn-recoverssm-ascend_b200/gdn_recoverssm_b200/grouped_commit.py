@@ -243,15 +243,11 @@ class GroupedCommitBucket:
         if len(host_rows) == rows and not all(0 <= r < limit for r in host_rows):
             raise ValueError("native request mapping exceeds the sampled batch")
 
-    def make_specs(self, entries, sampled, idx_mapping, persistent_cols, persistent_accepted, *, publish_align=True):
-        """Validate one step's entries and return the (plan, conv, fold)
-        launch specs without launching them (grouped_commit.py:670-893)."""
-        payloads, rows, align = self._step_payloads(entries, sampled, idx_mapping, persistent_cols,
-                                                    persistent_accepted)
-        ops = _native.ops()
-        groups = list(zip(payloads, self.contexts))
-        plan = _LaunchSpec("grouped_plan", ops.grouped_plan, (
-            sampled,
+    @staticmethod
+    def _group_lists(payloads, contexts, align):
+        """The grouped plan's per-group inputs, list by list."""
+        groups = list(zip(payloads, contexts))
+        return (
             [p.state_indices for p, _ in groups],
             [p.query_start_loc for p, _ in groups],
             [p.request_indices for p, _ in groups],
@@ -259,7 +255,16 @@ class GroupedCommitBucket:
             [p.num_computed_tokens if align else None for p, _ in groups],
             [int(c.num_blocks) for _, c in groups],
             [int(p.block_size) if align else 1 for p, _ in groups],
-            *(self.plan[i] for i in range(len(_PLAN_ROWS))),
+        )
+
+    def make_specs(self, entries, sampled, idx_mapping, persistent_cols, persistent_accepted, *, publish_align=True):
+        """Validate one step's entries and return the (plan, conv, fold)
+        launch specs without launching them (grouped_commit.py:670-893)."""
+        payloads, rows, align = self._step_payloads(entries, sampled, idx_mapping, persistent_cols,
+                                                    persistent_accepted)
+        ops = _native.ops()
+        plan = _LaunchSpec("grouped_plan", ops.grouped_plan, (
+            sampled, *self._group_lists(payloads, self.contexts, align), *self.plan,
             idx_mapping, persistent_cols if align else None, persistent_accepted if align else None,
             rows, self.capacity, self.spec_query_len, align, bool(align and publish_align),
         ))

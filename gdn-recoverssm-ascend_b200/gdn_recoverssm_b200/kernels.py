@@ -481,6 +481,47 @@ class GDNRecoverSSMCommitContext:
                    num_key_heads=heads, spec_query_len=spec_query_len, conv_history_len=history,
                    max_num_reqs=max_num_reqs)
 
+    def _fold_config(self, batch):
+        """The fold's 17 configuration fields for ``batch`` rows."""
+        ref, soa = self.checkpoints[0], self.record_layout == "soa"
+        record = self.replays[0]
+        rr = record.correction if soa else record
+        typed = (record.key.stride(1), record.key.stride(2), record.decay.stride(1), record.decay.stride(2)) \
+            if soa else (0, 0, 0, 0)
+        return [batch, len(self.checkpoints), ref.shape[1], self.num_key_heads, self.spec_query_len, self.num_blocks,
+                rr.shape[0], self.plan.shape[1], NULL_BLOCK_ID, ref.stride(1), ref.stride(2), rr.stride(1),
+                rr.stride(2), *typed]
+
+    def _record_args(self):
+        ref, soa = self.checkpoints[0], self.record_layout == "soa"
+        record = self.replays[0]
+        planes = (record.correction, record.key, record.decay) if soa else (record, record, record)
+        t = self.tables
+        return (ref, *planes, t["state_addr"], t["state_block"], t["corr_addr"], t["corr_block"], t["key_addr"],
+                t["key_block"], t["decay_addr"], t["decay_block"], self.layer_groups)
+
+    def _specs(self, accepted, request_indices, state_indices, qsl, block_table, computed, block_size,
+                     commit_conv):
+        """The step's launches: plan, conv compaction, fold; the conv compaction
+        and the fold are programmatic dependents of the launch before each."""
+        ops = _native.ops()
+        batch = state_indices.shape[0]
+        plan_rows = (self.commit_lens, self.final_state_indices, self.boundary_state_indices,
+                     self.boundary_recovery_lens)
+        specs = [_LaunchSpec("commit_plan", ops.commit_plan, (
+            accepted, request_indices, state_indices, qsl, block_table, computed, *self.plan, self.spec_query_len,
+            self.num_blocks, block_size))]
+        if commit_conv:
+            conv, t = self.conv_states[0], self.tables
+            specs.append(_LaunchSpec("compact_conv", ops.compact_conv, (
+                conv, t["conv_addr"], t["conv_block"], t["conv_dim"], t["conv_token"], self.layer_groups,
+                state_indices, *plan_rows, batch, self.plan.shape[1], int(conv.shape[1]), self.conv_history_len,
+                int(conv.shape[2]), self.num_blocks, block_table is not None)))
+        flags = 0 if self.record_layout == "soa" else _FOLD_PACKED
+        specs.append(_LaunchSpec("fold", ops.fold_ext, (
+            *self._record_args(), state_indices, *plan_rows, self._fold_config(batch), flags)))
+        return specs
+
     def make_commit_specs(self, num_accepted_tokens, state_indices, query_start_loc, request_indices=None,
                           block_table=None, num_computed_tokens=None, mamba_block_size=None,
                           commit_conv=True) -> tuple:
@@ -520,45 +561,9 @@ class GDNRecoverSSMCommitContext:
                                                          request_indices, block_table, num_computed_tokens)),
             "commit inputs must be on the same device",
         )
-        ops = _native.ops()
-        specs = []
-        specs.append(_LaunchSpec(
-            "commit_plan", ops.commit_plan,
-            (num_accepted_tokens, request_indices, state_indices, query_start_loc, block_table, num_computed_tokens,
-             self.commit_lens, self.final_state_indices, self.boundary_state_indices, self.boundary_recovery_lens,
-             self.align_valid, self.align_col, self.spec_query_len, self.num_blocks, int(mamba_block_size or 1)),
-        ))
-        layers = len(self.checkpoints)
-        if commit_conv:
-            conv = self.conv_states[0]
-            specs.append(_LaunchSpec(
-                "compact_conv", ops.compact_conv,
-                (conv, self.conv_state_base_addrs, self.conv_state_block_strides, self.conv_state_dim_strides,
-                 self.conv_state_token_strides, self.layer_groups, state_indices, self.commit_lens,
-                 self.final_state_indices, self.boundary_state_indices, self.boundary_recovery_lens, batch,
-                 self.commit_lens.shape[0], int(conv.shape[1]), self.conv_history_len, int(conv.shape[2]),
-                 self.num_blocks, block_table is not None),
-            ))
-        ref = self.checkpoints[0]
-        _, HV, V, K = ref.shape
-        soa = self.record_layout == "soa"
-        record = self.replays[0]
-        rr = record.correction if soa else record
-        kr = record.key if soa else record
-        dr = record.decay if soa else record
-        config = [
-            batch, layers, HV, self.num_key_heads, self.spec_query_len, self.num_blocks, rr.shape[0],
-            self.commit_lens.shape[0], NULL_BLOCK_ID, ref.stride(1), ref.stride(2), rr.stride(1), rr.stride(2),
-            kr.stride(1) if soa else 0, kr.stride(2) if soa else 0, dr.stride(1) if soa else 0,
-            dr.stride(2) if soa else 0,
-        ]
-        specs.append(_LaunchSpec(
-            "fold", ops.fold_ext,
-            (ref, rr, kr, dr, self.state_base_addrs, self.state_block_strides, self.correction_base_addrs,
-             self.correction_block_strides, self.key_base_addrs, self.key_block_strides, self.decay_base_addrs,
-             self.decay_block_strides, self.layer_groups, state_indices, self.commit_lens, self.final_state_indices,
-             self.boundary_state_indices, self.boundary_recovery_lens, config, 0 if soa else _FOLD_PACKED),
-        ))
+        plan_in = (num_accepted_tokens, request_indices, state_indices, query_start_loc, block_table,
+                   num_computed_tokens, int(mamba_block_size or 1))
+        specs = self._specs(*plan_in, commit_conv)
         if _collect is not None:
             _collect.extend(specs)
             return
