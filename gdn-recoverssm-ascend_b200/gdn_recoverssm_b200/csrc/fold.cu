@@ -6,14 +6,23 @@ GDN_RSSM_STATUS_WORD(fold)
 
 namespace gdn_rssm {
 
-template <int DIM, typename St, typename Kt>
+// CTAs per unit: fp32 tiles at K = V = 128 are folded in two 64-row halves.
+#ifndef GDN_RSSM_FOLD_PARTS
+#define GDN_RSSM_FOLD_PARTS 2
+#endif
+template <int DIM, typename St>
+constexpr int fold_parts() {
+  return (DIM == 128 && sizeof(St) == 4) ? GDN_RSSM_FOLD_PARTS : 1;
+}
+
+template <int DIM, typename St, typename Kt, int PARTS>
 int launch_fold_variant(FoldParams p, cudaStream_t stream) {
   p.status = status_ptr_for_device<symbol_fold>();
   if (p.status == nullptr) {
     set_error("GDN RecoverSSM: cannot resolve the device status word");
     return GDN_RSSM_ECUDA;
   }
-  constexpr int smem = fold_smem_bytes<DIM, St>();
+  constexpr int smem = fold_smem_bytes<DIM, St, PARTS>();
   static bool configured[64] = {false};
   int dev = 0;
   GDN_CUDA(cudaGetDevice(&dev));
@@ -22,16 +31,16 @@ int launch_fold_variant(FoldParams p, cudaStream_t stream) {
     return GDN_RSSM_EUNSUPPORTED;
   }
   if (!configured[dev]) {
-    GDN_CUDA(cudaFuncSetAttribute(fold_kernel<DIM, St, Kt>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    GDN_CUDA(cudaFuncSetAttribute(fold_kernel<DIM, St, Kt, PARTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev] = true;
   }
   // one CTA per (layer, row, value head) unit, launched as a programmatic
   // dependent of the kernel before it (the plan): its CTAs become resident
   // while the plan runs and wait in the kernel for the plan's results
-  const int64_t grid = p.layers * p.rows * p.heads;
+  const int64_t grid = p.layers * p.rows * p.heads * PARTS;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kFoldThreads);
+  cfg.blockDim = dim3(FoldShape<DIM, St, PARTS>::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -39,16 +48,16 @@ int launch_fold_variant(FoldParams p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  GDN_CUDA(cudaLaunchKernelEx(&cfg, fold_kernel<DIM, St, Kt>, p));
+  GDN_CUDA(cudaLaunchKernelEx(&cfg, fold_kernel<DIM, St, Kt, PARTS>, p));
   return GDN_RSSM_OK;
 }
 
 template <int DIM, typename St>
 int launch_fold_key(const FoldParams &p, int32_t key_dtype, cudaStream_t stream) {
   switch (key_dtype) {
-    case GDN_RSSM_F32: return launch_fold_variant<DIM, St, float>(p, stream);
-    case GDN_RSSM_BF16: return launch_fold_variant<DIM, St, __nv_bfloat16>(p, stream);
-    case GDN_RSSM_F16: return launch_fold_variant<DIM, St, __half>(p, stream);
+    case GDN_RSSM_F32: return launch_fold_variant<DIM, St, float, fold_parts<DIM, St>()>(p, stream);
+    case GDN_RSSM_BF16: return launch_fold_variant<DIM, St, __nv_bfloat16, fold_parts<DIM, St>()>(p, stream);
+    case GDN_RSSM_F16: return launch_fold_variant<DIM, St, __half, fold_parts<DIM, St>()>(p, stream);
   }
   set_error("GDN RecoverSSM: unsupported record key dtype");
   return GDN_RSSM_EUNSUPPORTED;

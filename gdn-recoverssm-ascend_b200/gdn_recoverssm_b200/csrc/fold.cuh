@@ -62,44 +62,52 @@ __device__ __forceinline__ uint4 pack16(const float *in, __nv_bfloat16) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <int DIM, typename St>
+// PARTS: the unit's V x K tile is folded by PARTS CTAs of DIM / PARTS state
+// rows each (kFoldThreads / PARTS threads): the same work per thread and per
+// SM in smaller pieces, so the last wave of a small batch is shorter.
+template <int DIM, typename St, int PARTS = 1>
 struct FoldShape {
+  static constexpr int ROWS = DIM / PARTS;                // state rows of one CTA
+  static constexpr int THREADS = kFoldThreads / PARTS;
   static constexpr int EPC = Chunk16<St>::N;             // state elements per 16-byte chunk
   static constexpr int CPR = DIM / EPC;                  // chunks per state row
-  static constexpr int RSTEP = kFoldThreads / CPR;       // rows between a thread's chunks
-  static constexpr int CPT = (DIM + RSTEP - 1) / RSTEP;  // chunks per thread (last may be empty)
-  static constexpr int TILE = DIM * DIM * sizeof(St);
-  static constexpr int CORR = kMaxWindow * DIM * 4;
+  static constexpr int RSTEP = THREADS / CPR;            // rows between a thread's chunks
+  static constexpr int CPT = (ROWS + RSTEP - 1) / RSTEP;  // chunks per thread (last may be empty)
+  static constexpr int TILE = ROWS * DIM * sizeof(St);
+  static constexpr int CORR = kMaxWindow * ROWS * 4;
   static constexpr int SMEM = 128 /* alignment slack */ + TILE + CORR + 64;
-  static_assert(kFoldThreads % CPR == 0, "fold layout");
+  static_assert(THREADS % CPR == 0 && DIM % PARTS == 0, "fold layout");
 };
 
-template <int DIM, typename St>
+template <int DIM, typename St, int PARTS = 1>
 constexpr int fold_smem_bytes() {
-  return FoldShape<DIM, St>::SMEM;
+  return FoldShape<DIM, St, PARTS>::SMEM;
 }
 
-// Three resident CTAs per SM; two for 2-byte state tiles, whose 8-wide key
-// slices need more registers.
-template <typename St>
+// Three resident CTAs per SM (times PARTS); two for 2-byte state tiles, whose
+// 8-wide key slices need more registers.
+template <typename St, int PARTS = 1>
 constexpr int fold_min_blocks() {
-  return sizeof(St) == 4 ? 3 : 2;
+  return (sizeof(St) == 4 ? 3 : 2) * PARTS;
 }
 
-template <int DIM, typename St, typename Kt>
-__global__ void __launch_bounds__(kFoldThreads, fold_min_blocks<St>()) fold_kernel(const FoldParams p) {
-  using Sh = FoldShape<DIM, St>;
-  constexpr int EPC = Sh::EPC, CPR = Sh::CPR, RSTEP = Sh::RSTEP, CPT = Sh::CPT;
+template <int DIM, typename St, typename Kt, int PARTS>
+__global__ void __launch_bounds__(FoldShape<DIM, St, PARTS>::THREADS, fold_min_blocks<St, PARTS>())
+    fold_kernel(const FoldParams p) {
+  using Sh = FoldShape<DIM, St, PARTS>;
+  constexpr int EPC = Sh::EPC, CPR = Sh::CPR, RSTEP = Sh::RSTEP, CPT = Sh::CPT, ROWS = Sh::ROWS;
+  constexpr int NT = Sh::THREADS;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
   unsigned char *tile = smem;
-  float(*s_corr)[DIM] = reinterpret_cast<float(*)[DIM]>(smem + Sh::TILE);
+  float(*s_corr)[ROWS] = reinterpret_cast<float(*)[ROWS]>(smem + Sh::TILE);
   float *s_decay = reinterpret_cast<float *>(smem + Sh::TILE + Sh::CORR);
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem + Sh::TILE + Sh::CORR + 32);
 
   const int64_t HV = p.heads;
-  const int64_t unit = blockIdx.x;
+  const int64_t unit = blockIdx.x / PARTS;
+  const int r0 = static_cast<int>(blockIdx.x % PARTS) * ROWS;  // first state row of this CTA
   const int head = static_cast<int>(unit % HV);
   const int64_t row = (unit / HV) % p.rows;
   const int64_t layer = unit / (HV * p.rows);
@@ -129,7 +137,7 @@ __global__ void __launch_bounds__(kFoldThreads, fold_min_blocks<St>()) fold_kern
     return;
   }
   const int tid = threadIdx.x;
-  const St *src_tile = state + src * sbs + head * p.state_hs;
+  const St *src_tile = state + src * sbs + head * p.state_hs + r0 * p.state_vs;
   if (tid < 32) {
     if (tid == 0) {
       ptx::mbar_init(bar, 1);
@@ -140,7 +148,7 @@ __global__ void __launch_bounds__(kFoldThreads, fold_min_blocks<St>()) fold_kern
     if (p.state_vs == DIM) {
       if (tid == 0) ptx::bulk_load(tile, src_tile, Sh::TILE, bar);
     } else {
-      for (int r = tid; r < DIM; r += 32)
+      for (int r = tid; r < ROWS; r += 32)
         ptx::bulk_load(tile + r * DIM * sizeof(St), src_tile + r * p.state_vs, DIM * sizeof(St), bar);
     }
   }
@@ -164,20 +172,21 @@ __global__ void __launch_bounds__(kFoldThreads, fold_min_blocks<St>()) fold_kern
   }
   const int col = tid % CPR;    // fixed 16-byte column chunk of this thread
   const int rbase = tid / CPR;  // rows rbase, rbase + RSTEP, ...
-  float cv[kMaxWindow * DIM / kFoldThreads + 1];
+  float cv[kMaxWindow * ROWS / NT + 1];
   {
-    // issue every record load before any store (one memory round trip)
-    constexpr int PER = (kMaxWindow * DIM + kFoldThreads - 1) / kFoldThreads;
+    // issue every record load before any store (one memory round trip); the
+    // corrections of this CTA's rows only
+    constexpr int PER = (kMaxWindow * ROWS + NT - 1) / NT;
 #pragma unroll
     for (int c = 0; c < PER; ++c) {
-      const int idx = tid + c * kFoldThreads;
-      const int t = idx / DIM, e = idx % DIM;
-      cv[c] = (t < n) ? corr[t * p.corr_ts + e] : 0.f;
+      const int idx = tid + c * NT;
+      const int t = idx / ROWS, e = idx % ROWS;
+      cv[c] = (t < n) ? corr[t * p.corr_ts + r0 + e] : 0.f;
     }
 #pragma unroll
     for (int c = 0; c < PER; ++c) {
-      const int idx = tid + c * kFoldThreads;
-      const int t = idx / DIM, e = idx % DIM;
+      const int idx = tid + c * NT;
+      const int t = idx / ROWS, e = idx % ROWS;
       if (t < n) s_corr[t][e] = cv[c];
     }
   }
@@ -196,12 +205,12 @@ __global__ void __launch_bounds__(kFoldThreads, fold_min_blocks<St>()) fold_kern
     ptx::mbar_wait_bounded(bar, 0, kFoldWaitLimitNs);  // let an in-flight copy land before exiting
     return;
   }
-  St *fin_tile = state + fin * sbs + head * p.state_hs;
-  St *b_tile = state + bidx * sbs + head * p.state_hs;
+  St *fin_tile = state + fin * sbs + head * p.state_hs + r0 * p.state_vs;
+  St *b_tile = state + bidx * sbs + head * p.state_hs + r0 * p.state_vs;
 #pragma unroll 4
   for (int i = 0; i < CPT; ++i) {
-    const int r = rbase + i * RSTEP;
-    if (DIM % RSTEP != 0 && r >= DIM) break;
+    const int r = rbase + i * RSTEP;  // row of this CTA's slab
+    if (ROWS % RSTEP != 0 && r >= ROWS) break;
     const uint4 raw = *reinterpret_cast<const uint4 *>(tile + (r * DIM + col * EPC) * sizeof(St));
     float h[EPC];
     unpack16(raw, h, St());
