@@ -429,6 +429,8 @@ def run_b200(args):
     vbytes = synthetic.verify_bytes(wl)
     fbytes = synthetic.commit_bytes(wl, lens, int(bnd.sum()))
     cbytes = synthetic.conv_bytes(wl, lens, int(bnd.sum()), ctx.conv_history_len) if conv else 0
+    cfloor = synthetic.conv_floor_bytes(wl, lens, wl.state_indices[: wl.B].cpu(), ctx.final_state_indices[: wl.B].cpu(),
+                                        ctx.boundary_state_indices[: wl.B].cpu(), bnd) if conv else 0
     verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
     step_gbs = (vbytes + fbytes + cbytes) / (step_ms * 1e-3) / 1e9
     kernels = {"verify": {"ms": verify_ms, "bytes": vbytes, "GB/s": verify_gbs, "frac": verify_gbs / peak}}
@@ -438,6 +440,10 @@ def run_b200(args):
         if name in bytes_of:
             gbs = bytes_of[name] / (ms * 1e-3) / 1e9
             kernels[name].update({"bytes": bytes_of[name], "GB/s": gbs, "frac": gbs / peak})
+    if conv:
+        # the sector floor of the dim-first conv pool: what the layout makes any kernel move
+        gbs = cfloor / (spec_ms["compact_conv"] * 1e-3) / 1e9
+        kernels["compact_conv"].update({"sector_floor_bytes": cfloor, "floor_GB/s": gbs, "floor_frac": gbs / peak})
     kernels["step"] = {"GB/s": step_gbs, "frac": step_gbs / peak, "per_rank_bytes": vbytes + fbytes + cbytes}
     top = "fold"  # the largest byte mover
     reduced = args.rows is not None or args.pool is not None or bool(args.shard_of) or conv

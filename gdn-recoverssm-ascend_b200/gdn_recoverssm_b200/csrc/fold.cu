@@ -128,18 +128,29 @@ int launch_compact_conv(const ConvParams &params, int elem_size, cudaStream_t st
   const unsigned smem = p.vec ? static_cast<unsigned>(3 * p.chunk * row_bytes) : 0u;
   // x: (layer, row); y: chunks of channels
   const dim3 grid(static_cast<unsigned>(p.layers * p.rows), static_cast<unsigned>((p.conv_dim + p.chunk - 1) / p.chunk));
-  static bool carveout[2][64] = {};  // shared memory first: six 36 KB CTAs per SM, not three
+  p.status = status_ptr_for_device<symbol_fold>();
+  if (p.status == nullptr) {
+    set_error("GDN RecoverSSM: cannot resolve the device status word");
+    return GDN_RSSM_ECUDA;
+  }
+  // shared memory first (four 48 KB CTAs per SM), and room for the staging
+  // chunks beside the kernel's static mbarrier
+  static bool configured[2][64] = {};
   int dev = 0;
   GDN_CUDA(cudaGetDevice(&dev));
-  if (dev >= 0 && dev < 64 && (elem_size == 2 || elem_size == 4) && !carveout[elem_size / 4][dev]) {
+  if (dev >= 0 && dev < 64 && (elem_size == 2 || elem_size == 4) && !configured[elem_size / 4][dev]) {
     if (elem_size == 2) {
       GDN_CUDA(cudaFuncSetAttribute(compact_conv_kernel<uint16_t>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     cudaSharedmemCarveoutMaxShared));
+      GDN_CUDA(cudaFuncSetAttribute(compact_conv_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kConvSmemLimit));
     } else {
       GDN_CUDA(cudaFuncSetAttribute(compact_conv_kernel<uint32_t>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     cudaSharedmemCarveoutMaxShared));
+      GDN_CUDA(cudaFuncSetAttribute(compact_conv_kernel<uint32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kConvSmemLimit));
     }
-    carveout[elem_size / 4][dev] = true;
+    configured[elem_size / 4][dev] = true;
   }
   switch (elem_size) {  // a programmatic dependent of the plan, as the fold behind it is of this kernel
     case 2: return launch_dependent(compact_conv_kernel<uint16_t>, p, grid, kConvThreads, stream, smem);

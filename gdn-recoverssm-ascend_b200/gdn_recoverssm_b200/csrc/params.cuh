@@ -57,6 +57,7 @@ struct ConvParams {
   int32_t chunk;      // channels per CTA (blockIdx.y)
   int32_t vec;        // 1: stage whole chunks through shared memory with 16-byte copies
   int32_t elem_size;  // bytes per conv element (2 or 4)
+  int32_t *status;    // device status word of the fold translation unit
 };
 
 }  // namespace gdn_rssm

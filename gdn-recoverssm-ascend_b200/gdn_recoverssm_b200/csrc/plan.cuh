@@ -26,6 +26,7 @@ constexpr int kMaxConvHistory = 8;
 constexpr int kConvThreads = 256;
 constexpr int kConvChannelsPerCta = 1024;  // largest chunk
 constexpr int kConvSmemLimit = 48 * 1024;  // staging of the contiguous path: 3 chunks
+constexpr uint64_t kConvWaitLimitNs = 1000000000ull;  // 1 s
 
 
 // 32-bit two's-complement arithmetic of the per-context plan: the reference
@@ -246,8 +247,34 @@ __global__ void publish_align_kernel(const PublishParams p) {
 // One CTA per (layer, row); threads stride over the [conv_dim, history] window.
 // Both windows are read into registers before either is stored (the final or
 // the boundary page may alias the source page).
+// dst[h] = src[from + h] for h < hist (element stride ts), ascending: safe in
+// place (dst == src) because every read (from + h >= h) is at or ahead of
+// the writes already done.
 template <typename E>
-__global__ void __launch_bounds__(kConvThreads, 6) compact_conv_kernel(const ConvParams p) {
+__device__ __forceinline__ void shift_window(E *dst, const E *src, int64_t from, int hist, int64_t ts) {
+#pragma unroll 1
+  for (int h = 0; h < hist; ++h) dst[h * ts] = src[(from + h) * ts];
+}
+
+// The history windows of one channel: boundary snapshot (when do_b) and final
+// window, both taken from the source rows as they were before either store.
+// A target that aliases the source is written last (ascending, in place); a
+// boundary on the final page is overwritten by the final window, so it is not
+// written at all.
+template <typename E>
+__device__ __forceinline__ void compact_channel(E *fin_row, E *bnd_row, const E *src_row, int32_t n, int32_t blen,
+                                                bool do_b, bool bnd_is_src, bool bnd_is_fin, int hist, int64_t ts) {
+  if (do_b && bnd_is_src && !bnd_is_fin) {
+    shift_window(fin_row, src_row, n - 1, hist, ts);
+    shift_window(bnd_row, src_row, blen - 1, hist, ts);
+  } else {
+    if (do_b && !bnd_is_fin) shift_window(bnd_row, src_row, blen - 1, hist, ts);
+    shift_window(fin_row, src_row, n - 1, hist, ts);
+  }
+}
+
+template <typename E>
+__global__ void __launch_bounds__(kConvThreads, 4) compact_conv_kernel(const ConvParams p) {
   ptx::wait_prerequisite_grid();  // launched as a dependent of the plan: its results first
   ptx::launch_dependents();       // the fold may start launching (it waits for this grid)
   const int64_t row = blockIdx.x % p.rows;
@@ -275,78 +302,61 @@ __global__ void __launch_bounds__(kConvThreads, 6) compact_conv_kernel(const Con
   const int64_t d0 = static_cast<int64_t>(blockIdx.y) * p.chunk;
   const int64_t nch = p.conv_dim - d0 < p.chunk ? p.conv_dim - d0 : p.chunk;
   if (nch <= 0) return;
+  const bool bnd_is_src = do_b && bidx == src;
+  const bool bnd_is_fin = do_b && bidx == fin;  // the final window overwrites it: not stored separately
   const int64_t W = p.window;
+  const uint32_t bytes = static_cast<uint32_t>(nch * W * static_cast<int64_t>(sizeof(E)));
   const bool aligned = ((reinterpret_cast<uintptr_t>(srcp + d0 * W) | reinterpret_cast<uintptr_t>(finp + d0 * W) |
-                         reinterpret_cast<uintptr_t>(bndp + d0 * W)) & 15) == 0;
+                         reinterpret_cast<uintptr_t>(bndp + d0 * W) | bytes) & 15) == 0;
   if (p.vec && ts == 1 && ds == W && aligned) {
-    // Contiguous windows: the chunk's rows of the source, final and boundary
-    // pages come into shared memory with 16-byte copies, the history windows
-    // move there, and the final / boundary chunks go back whole -- full-sector
-    // traffic instead of 2-byte accesses.  Every read precedes every store,
-    // so pages that alias (in place, boundary == source) behave as above.
+    // Contiguous windows: the chunk's rows of each distinct page (source,
+    // final, boundary) come into shared memory with one bulk copy each, the
+    // history windows move there, and the final / boundary chunks go back
+    // with one bulk store each -- full-sector traffic and a few instructions
+    // per CTA.  A page that is the source (in place, or a boundary aliasing
+    // the source) is read once.  Every read lands before any store.
     extern __shared__ __align__(16) unsigned char conv_smem[];
+    __shared__ uint64_t bar;
     E *sA = reinterpret_cast<E *>(conv_smem);
     E *sB = sA + static_cast<int64_t>(p.chunk) * W;
     E *sC = sB + static_cast<int64_t>(p.chunk) * W;
-    // 32-bit indices inside a chunk (at most 48 KB of shared memory)
-    const int w = static_cast<int>(W), nc = static_cast<int>(nch);
-    const int elems = nc * w;
-    const int nvec = elems * static_cast<int>(sizeof(E)) / 16;
-    const int tail0 = nvec * 16 / static_cast<int>(sizeof(E));
+    const bool fin_is_src = fin == src;
+    E *t_fin = fin_is_src ? sA : sB;
+    E *t_bnd = bnd_is_src ? sA : sC;
     const int tid = threadIdx.x;
-    auto copy_in = [&](E *dst, const E *src) {  // asynchronous 16-byte copies (cp.async), no register round trip
-      for (int i = tid; i < nvec; i += kConvThreads)
-        ptx::cp_async16(reinterpret_cast<uint4 *>(dst) + i, reinterpret_cast<const uint4 *>(src) + i);
-      for (int i = tail0 + tid; i < elems; i += kConvThreads) dst[i] = src[i];
-    };
-    auto copy_out = [&](E *dst, const E *src) {
-      for (int i = tid; i < nvec; i += kConvThreads)
-        reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
-      for (int i = tail0 + tid; i < elems; i += kConvThreads) dst[i] = src[i];
-    };
-    copy_in(sA, srcp + d0 * W);
-    copy_in(sB, finp + d0 * W);
-    if (do_b) copy_in(sC, bndp + d0 * W);
-    ptx::cp_async_commit();
-    ptx::cp_async_wait_all();
-    __syncthreads();
-    for (int c = tid; c < nc; c += kConvThreads) {
-      const E *a = sA + c * w;
-      E *b = sB + c * w;
-      for (int h = 0; h < hist; ++h) b[h] = a[n - 1 + h];
-      if (do_b) {
-        E *cc = sC + c * w;
-        for (int h = 0; h < hist; ++h) cc[h] = a[blen - 1 + h];
-      }
+    if (tid == 0) {
+      const uint32_t loads = 1 + (fin_is_src ? 0 : 1) + (do_b && !bnd_is_src && !bnd_is_fin ? 1 : 0);
+      ptx::mbar_init(&bar, 1);
+      ptx::fence_mbar_init();
+      ptx::mbar_arrive_expect_tx(&bar, loads * bytes);
+      ptx::bulk_load(sA, srcp + d0 * W, bytes, &bar);
+      if (!fin_is_src) ptx::bulk_load(sB, finp + d0 * W, bytes, &bar);
+      if (do_b && !bnd_is_src && !bnd_is_fin) ptx::bulk_load(sC, bndp + d0 * W, bytes, &bar);
     }
+    __syncthreads();  // barrier initialised
+    if (!ptx::mbar_wait_bounded(&bar, 0, kConvWaitLimitNs)) {
+      if (tid == 0) atomicExch(p.status, kStatusTmaTimeout);
+      ptx::mbar_wait_bounded(&bar, 0, kConvWaitLimitNs);  // let an in-flight copy land before exiting
+      return;
+    }
+    const int w = static_cast<int>(W), nc = static_cast<int>(nch);
+    for (int c = tid; c < nc; c += kConvThreads)
+      compact_channel(t_fin + c * w, t_bnd + c * w, sA + c * w, n, blen, do_b, bnd_is_src, bnd_is_fin, hist, 1);
+    ptx::fence_proxy_async_smem();  // the composed rows -> the bulk stores' reads
     __syncthreads();
-    if (do_b) copy_out(bndp + d0 * W, sC);  // same thread per address as the final copy: final lands last
-    copy_out(finp + d0 * W, sB);
+    if (tid == 0) {
+      if (do_b && !bnd_is_fin) ptx::bulk_store(bndp + d0 * W, t_bnd, bytes);
+      ptx::bulk_store(finp + d0 * W, t_fin, bytes);
+      ptx::bulk_commit();
+      ptx::bulk_wait_read();  // shared memory stays valid until the stores have read it
+    }
     return;
   }
-  // General strides: one thread per channel; it reads both windows of its
-  // channel before it stores either (boundary first, then final), and no two
-  // threads touch the same channel, so an in-place row (final or boundary ==
-  // source) needs no barrier.
-  for (int64_t d = d0 + threadIdx.x; d < d0 + nch; d += blockDim.x) {
-    const E *sd = srcp + d * ds;
-    E fv[kMaxConvHistory], bv[kMaxConvHistory];
-#pragma unroll
-    for (int h = 0; h < kMaxConvHistory; ++h) {
-      if (h < hist) {
-        fv[h] = sd[(n - 1 + h) * ts];
-        if (do_b) bv[h] = sd[(blen - 1 + h) * ts];
-      }
-    }
-    if (do_b) {
-#pragma unroll
-      for (int h = 0; h < kMaxConvHistory; ++h)
-        if (h < hist) bndp[d * ds + h * ts] = bv[h];
-    }
-#pragma unroll
-    for (int h = 0; h < kMaxConvHistory; ++h)
-      if (h < hist) finp[d * ds + h * ts] = fv[h];
-  }
+  // General strides: one thread per channel; no two threads touch the same
+  // channel, so an in-place row (final or boundary == source) needs no barrier.
+#pragma unroll 1
+  for (int64_t d = d0 + threadIdx.x; d < d0 + nch; d += blockDim.x)
+    compact_channel(finp + d * ds, bndp + d * ds, srcp + d * ds, n, blen, do_b, bnd_is_src, bnd_is_fin, hist, ts);
 }
 
 }  // namespace gdn_rssm

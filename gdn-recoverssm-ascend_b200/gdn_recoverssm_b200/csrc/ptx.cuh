@@ -116,6 +116,19 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, u
 namespace gdn_rssm {
 namespace ptx {
 
+// Untiled bulk copy shared -> global (16-byte aligned addresses, size a
+// multiple of 16), tracked by this thread's bulk async-group; make generic
+// shared-memory writes visible to it first (fence_proxy_async_smem).
+__device__ __forceinline__ void bulk_store(void *dst, const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_addr(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has read its shared
+// memory (the buffers may then be reused or the CTA may exit).
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // Untiled bulk copy global -> shared (16-byte aligned addresses, size a
 // multiple of 16), completion signalled on `bar`.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

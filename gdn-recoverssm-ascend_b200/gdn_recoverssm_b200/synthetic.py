@@ -263,6 +263,24 @@ def conv_bytes(wl: Workload, lengths, boundary_written, history: int) -> int:
     return (working + int(boundary_written)) * per
 
 
+def conv_floor_bytes(wl: Workload, lengths, source, final, boundary, boundary_written) -> int:
+    """Bytes one conv compaction must move in a dim-first pool, whose channel
+    windows are adjacent W-element rows: the history positions of every row
+    cover every 32-byte sector of a page's channel block, and stores of the
+    first ``history`` positions leave the rest of each sector to be preserved.
+    Per working row: the source block read, the final block read and written
+    (written only, in place), and per boundary snapshot the boundary block
+    read and written (written only, when it is the source page)."""
+    n = torch.as_tensor(lengths).long()
+    src, fin, bnd = (torch.as_tensor(t).long() for t in (source, final, boundary))
+    written = torch.as_tensor(boundary_written).bool()
+    work = n > 0
+    page = wl.conv.shape[1] * wl.conv.shape[2] * wl.conv.element_size()
+    blocks = work.sum() + (work & (fin != src)).sum() * 2 + (work & (fin == src)).sum()
+    blocks += (work & written & (bnd != src)).sum() * 2 + (work & written & (bnd == src)).sum()
+    return int(blocks) * page
+
+
 def commit_bytes(wl: Workload, lengths, boundary_written) -> int:
     """Algorithmic bytes of one fold call: state read + final write (+ the
     boundary snapshot where one is written) + the accepted records read."""
