@@ -8,8 +8,9 @@ Q=4, prefix-cache align mode with 64-token blocks, bf16 q/k/v, fp32 state pool
 of 4096 pages, packed fp32 records).  Synthetic, seeded inputs of those
 shapes.  `--gated` verifies through the fused-gating entry point.
 
-The headline loop issues the steps back to back with nothing between the
-launches; a second pass with CUDA events between the launches gives the
+The headline loop replays the steps back to back from a CUDA graph of whole
+steps (`--launch eager` issues each step from Python instead), nothing between
+the launches; a second pass with CUDA events between the launches gives the
 per-kernel split.  `e2e` repeats the step through the public API with the
 inputs copied from pinned host memory and the output copied back, every step.
 `--impl reference` times the CPU restatement of the reference's path
@@ -376,11 +377,26 @@ def run_b200(args):
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
+    def step():
         verify()
         for sp in specs:
             sp.launch()
+
+    for _ in range(args.warmup):
+        step()
     barrier()
+    graph, gsteps = None, 1
+    if args.launch == "graph":
+        # the headline steps replayed from a CUDA graph of `gsteps` whole steps
+        # (verify + every commit launch, programmatic dependencies kept), as a
+        # serving loop replays its decode step: no host work per step
+        gsteps = next(d for d in (10, 5, 4, 2, 1) if args.steps % d == 0)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(gsteps):
+                step()
+        graph.replay()
+        barrier()
     # plan outputs are identical every step (same metadata): byte model inputs
     lens = ctx.commit_lens[: wl.B].cpu()
     bnd = ((ctx.boundary_state_indices[: wl.B] > 0) & (ctx.boundary_recovery_lens[: wl.B] > 0)
@@ -392,12 +408,16 @@ def run_b200(args):
         # (each commit launch is a programmatic dependent of the kernel before it)
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
+        host_t0 = time.perf_counter()
         t_start.record(stream)
-        for i in range(args.steps):
-            verify()
-            for sp in specs:
-                sp.launch()
+        if graph is not None:
+            for _ in range(args.steps // gsteps):
+                graph.replay()
+        else:
+            for i in range(args.steps):
+                step()
         t_end.record(stream)
+        host_issue_ms = (time.perf_counter() - host_t0) * 1e3 / args.steps
         barrier()
         # the same steps again with an event between launches: per-kernel times
         for i in range(args.steps):
@@ -420,6 +440,7 @@ def run_b200(args):
     step_ms, e2e_ms, verify_ms, spec_ms = timings[0], timings[1], timings[2], dict(zip(names, timings[3:]))
     clk = clocks.summary()
     status = int(torch.ops.gdn_recoverssm_ac.device_status())
+    graphed, graph = graph is not None, None  # released before the process group
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -466,6 +487,9 @@ def run_b200(args):
         "device_status": status,
     }
     line["config"]["commit_launches"] = names
+    line["config"]["launch"] = (f"CUDA graph of {gsteps} steps, replayed" if graphed
+                                else "eager: each step issued from Python")
+    line["host_issue_ms_per_step"] = host_issue_ms
     if args.shard_of:
         line["config"]["parallelism"] = f"rank 0 of a {args.shard_of}-way v-head split, on one GPU (profiling only)"
     if conv:
@@ -583,6 +607,8 @@ def main(argv=None):
                     help="verify through the fused-gating entry point (raw a, b, A_log, dt_bias)")
     ap.add_argument("--e2e-buffers", type=int, default=3, help="device input/output buffers of the end-to-end loop")
     ap.add_argument("--e2e-steps", type=int, default=50, help="fewest steps the end-to-end pass times")
+    ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
+                    help="headline steps replayed from a CUDA graph, or issued one by one from Python")
     ap.add_argument("--rows", type=int, default=None, help="reduced batch (profiling cases only)")
     ap.add_argument("--shard-of", type=int, default=0,
                     help="one GPU runs rank 0's head shard of an N-way split (profiling the per-rank step only)")
