@@ -253,9 +253,16 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 // the data has arrived.
 template <int NCOL>
 __device__ __forceinline__ void tmem_ld_sync(uint32_t taddr, float *v) {
-  static_assert(NCOL == 16 || NCOL == 32, "tcgen05.ld width");
+  static_assert(NCOL == 8 || NCOL == 16 || NCOL == 32, "tcgen05.ld width");
   uint32_t r[NCOL];
-  if constexpr (NCOL == 16) {
+  if constexpr (NCOL == 8) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+  } else if constexpr (NCOL == 16) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
         "tcgen05.wait::ld.sync.aligned;"

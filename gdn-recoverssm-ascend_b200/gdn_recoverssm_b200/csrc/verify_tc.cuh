@@ -16,7 +16,9 @@
 //   pass 2 (8 x kind::f16, A = bf16(lo(S)) written by the threads into tensor
 //          memory, B = bf16(X)) adds lo(S) X in its own columns.
 // Column j + column 2Q + j of pass 1 plus column j of pass 2 is the row's j-th
-// dot product; the dropped terms are below 2^-19 relative.
+// dot product; the dropped terms are below 2^-19 relative.  With exact
+// operands (lo(X) = 0) pass 1 holds hi(S) X alone and pass 2 accumulates onto
+// those columns, so column j is the dot product.
 //
 // Grid: up to three CTAs (256 threads) per SM (two at Q = 8), each walking the
 // units blockIdx.x, blockIdx.x + gridDim.x, ...; per unit:
@@ -61,7 +63,8 @@ struct VerifyTcShape {
   static constexpr int NB = (XROWS + 15) / 16 * 16;    // ... padded with zero rows to the MMA's N
   static constexpr int TMEM_COLS = 128;
   static constexpr uint32_t D_COL = 0;                 // pass-1 accumulator: NB columns
-  static constexpr uint32_t D2_COL = 32;               // pass-2 accumulator: 16 columns
+  static constexpr uint32_t D2_COL = 32;               // pass-2 accumulator: 16 columns (split operands)
+  static constexpr int NLD = NJ <= 8 ? 8 : 16;         // accumulator columns read back (exact operands)
   static constexpr uint32_t A_LO = 64;                 // bf16 lo(S): 64 columns of packed pairs
   static constexpr int NB2 = 16;                       // pass-2 N (minimum for M = 128)
   static constexpr int G2 = (NJ + 7) / 8;              // 8-row groups of bf16(X) that hold data
@@ -633,7 +636,11 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
 #pragma unroll
         for (int kk = 0; kk < DIM / 16; ++kk) {
           const uint64_t b = ptx::sw128_kmajor_desc(b2_addr + (kk >> 2) * Sh::B2_SLAB + (kk & 3) * 32);
-          ptx::mma_bf16_ts(tmem + Sh::D2_COL, tmem + Sh::A_LO + kk * 8, b, IDESC2, kk > 0);
+          // exact operands: onto pass 1's sums (in issue order); split: own columns
+          if constexpr (EXACT)
+            ptx::mma_bf16_ts(tmem + Sh::D_COL, tmem + Sh::A_LO + kk * 8, b, IDESC2, true);
+          else
+            ptx::mma_bf16_ts(tmem + Sh::D2_COL, tmem + Sh::A_LO + kk * 8, b, IDESC2, kk > 0);
         }
         ptx::mma_commit(&sm.mma_bar);
       }
@@ -662,8 +669,12 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       float d[NB], d2[16];
       __syncwarp();  // tcgen05.ld is warp-wide (.sync.aligned)
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-      ptx::tmem_ld_sync<NB>(lane_base + Sh::D_COL, d);
-      ptx::tmem_ld_sync<16>(lane_base + Sh::D2_COL, d2);
+      if constexpr (EXACT) {
+        ptx::tmem_ld_sync<Sh::NLD>(lane_base + Sh::D_COL, d);  // the data columns only
+      } else {
+        ptx::tmem_ld_sync<NB>(lane_base + Sh::D_COL, d);
+        ptx::tmem_ld_sync<16>(lane_base + Sh::D2_COL, d2);
+      }
       ptx::tc_fence_before_sync();
       const bool writer_corr = warp < 4;
       float cr[QT];
@@ -671,14 +682,14 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       for (int t = 0; t < QT; ++t) {
         cr[t] = 0.f;
         if (!((vmask >> t) & 1)) continue;
-        float kv = w.A[t] * (EXACT ? d[t] + d2[t] : (d[t] + d[NJ + t]) + d2[t]);
+        float kv = w.A[t] * (EXACT ? d[t] : (d[t] + d[NJ + t]) + d2[t]);
 #pragma unroll
         for (int s2 = 0; s2 < t; ++s2) kv = fmaf(w.mkk[t][s2], cr[s2], kv);
         cr[t] = w.beta[t] * (to_f32<Act>(ic.v[t]) - kv);
         if (writer_corr) {
           if (rec_ok) p.corr[row * p.corr_rs + hv * p.corr_hs + t * p.corr_ts + r] = cr[t];
         } else {
-          float o = w.A[t] * (EXACT ? d[QT + t] + d2[QT + t] : (d[QT + t] + d[NJ + QT + t]) + d2[QT + t]);
+          float o = w.A[t] * (EXACT ? d[QT + t] : (d[QT + t] + d[NJ + QT + t]) + d2[QT + t]);
 #pragma unroll
           for (int s2 = 0; s2 <= t; ++s2) o = fmaf(w.mkq[t][s2], cr[s2], o);
           if constexpr (EXACT) o *= p.scale;
