@@ -52,6 +52,16 @@
 
 namespace gdn_rssm {
 
+// A unit's row metadata, reduced to 32-bit fields when it is loaded (the host
+// keeps rows, tokens and blocks below 2^31): the token mask holds the window's
+// masking (t < Q, t < qlen, 0 <= bos + t < tokens), so bos only addresses valid
+// tokens and always fits; slot is -1 for a null or out-of-pool page.  Small
+// fields matter here: every register the walk keeps across units counts
+// against the 80 that three resident CTAs leave per thread.
+struct TcUnitMeta {
+  int32_t bos, slot, vmask;
+};
+
 // EXACT: the window's vectors are exact tf32 values (bf16 / fp16 inputs used as
 // they are, no in-kernel normalisation, q unscaled), so lo(X) = 0 and the
 // pass-1 operand holds X alone; the output is scaled after the dot products.
@@ -89,9 +99,12 @@ struct VerifyTcShape {
     uint64_t tile_bar;
     uint64_t mma_bar;
     // bos, eos, slot of the unit two ahead, as copied (cp.async), by the
-    // parity of the walk step that copied them: a warp still decoding step
-    // i's copy never races the copy step i + 1 starts before any barrier
+    // parity of the walk step that copied them, and the same decoded by the
+    // copying thread once its copy has landed (read by everyone after the
+    // next CTA barrier): a slow warp still reading step i's entry never races
+    // the copy that step i + 1 starts before any barrier
     uint64_t meta_raw[2][3];
+    TcUnitMeta meta[2];
     uint32_t tmem;
     float gpart[4][QT * QT];  // Gram partial sums per K slab
     Window win[2];
@@ -259,15 +272,6 @@ struct TcCursor {
   }
 };
 
-// A unit's row metadata, reduced to 32-bit fields when it is loaded (the host
-// keeps rows, tokens and blocks below 2^31): the token mask holds the window's
-// masking (t < Q, t < qlen, 0 <= bos + t < tokens), so bos only addresses valid
-// tokens and always fits; slot is -1 for a null or out-of-pool page.  Small
-// fields matter here: every register the walk keeps across units counts
-// against the 80 that three resident CTAs leave per thread.
-struct TcUnitMeta {
-  int32_t bos, slot, vmask;
-};
 
 __device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int64_t slot, int QT, int64_t Q,
                                                    int64_t tokens, int64_t null_block, int64_t blocks) {
@@ -478,8 +482,11 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       }
       // the next unit's tile (this unit started none)
       if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
-      if (tid == kMetaThread) ptx::cp_async_wait_all();
-      __syncthreads();  // the previous unit's recurrence is done with its window buffer; metadata copied
+      if (tid == kMetaThread) {
+        ptx::cp_async_wait_all();
+        sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1]);
+      }
+      __syncthreads();  // the previous unit's recurrence is done with its window buffer; metadata decoded
     } else {
       // ---- stage the window --------------------------------------------------- //
       // decay and beta of the window -> shared memory (read after the next CTA
@@ -654,7 +661,10 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           w.A[t] = a;
         }
       }
-      if (tid == kMetaThread) ptx::cp_async_wait_all();  // the copies started a phase ago
+      if (tid == kMetaThread) {  // the copies started a phase ago: decoded once, for everyone
+        ptx::cp_async_wait_all();
+        sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1]);
+      }
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
         if (tid == 0) atomicExch(p.status, kStatusMmaTimeout);
         ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs);
@@ -676,30 +686,42 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         ptx::tmem_ld_sync<16>(lane_base + Sh::D2_COL, d2);
       }
       ptx::tc_fence_before_sync();
-      const bool writer_corr = warp < 4;
+      // The chain runs over every token without a mask test: a masked token
+      // has beta = 0 and zero k / v rows (so zero Gram terms), its
+      // correction comes out as a signed zero and adds nothing to the later
+      // tokens -- the live tokens' arithmetic is unchanged.  Only the stores
+      // test the mask.
       float cr[QT];
 #pragma unroll
       for (int t = 0; t < QT; ++t) {
-        cr[t] = 0.f;
-        if (!((vmask >> t) & 1)) continue;
         float kv = w.A[t] * (EXACT ? d[t] : (d[t] + d[NJ + t]) + d2[t]);
 #pragma unroll
         for (int s2 = 0; s2 < t; ++s2) kv = fmaf(w.mkk[t][s2], cr[s2], kv);
         cr[t] = w.beta[t] * (to_f32<Act>(ic.v[t]) - kv);
-        if (writer_corr) {
-          if (rec_ok) p.corr[row * p.corr_rs + hv * p.corr_hs + t * p.corr_ts + r] = cr[t];
-        } else {
+      }
+      if (warp < 4) {  // correction records
+        if (rec_ok) {
+          float *cp = p.corr + row * p.corr_rs + hv * p.corr_hs + r;
+#pragma unroll
+          for (int t = 0; t < QT; ++t)
+            if ((vmask >> t) & 1) cp[t * p.corr_ts] = cr[t];
+        }
+      } else {  // outputs
+        Act *op = out + static_cast<int64_t>(m0.bos) * p.out_ts + hv * DIM + r;
+#pragma unroll
+        for (int t = 0; t < QT; ++t) {
+          if (!((vmask >> t) & 1)) continue;
           float o = w.A[t] * (EXACT ? d[QT + t] : (d[QT + t] + d[NJ + QT + t]) + d2[QT + t]);
 #pragma unroll
           for (int s2 = 0; s2 <= t; ++s2) o = fmaf(w.mkq[t][s2], cr[s2], o);
           if constexpr (EXACT) o *= p.scale;
-          out[(static_cast<int64_t>(m0.bos) + t) * p.out_ts + hv * DIM + r] = from_f32<Act>(o);
+          op[t * p.out_ts] = from_f32<Act>(o);
         }
       }
     }
     ic = in;
     m0 = m1;
-    m1 = decode_meta(sm.meta_raw[i & 1]);  // copied before the last CTA barrier
+    m1 = sm.meta[i & 1];  // decoded before the last CTA barrier
     c0 = c1;
     c1 = c2;
     c2.advance(dq, dr, HV32);
