@@ -59,7 +59,10 @@ namespace gdn_rssm {
 // fields matter here: every register the walk keeps across units counts
 // against the 80 that three resident CTAs leave per thread.
 struct TcUnitMeta {
-  int32_t bos, slot, vmask;
+  int32_t bos, slot;
+  int32_t vk;  // token mask (bits 0-7) | the key head the value head reads << 8
+  __device__ __forceinline__ int vmask() const { return vk & 0xff; }
+  __device__ __forceinline__ int kh() const { return vk >> 8; }
 };
 
 // EXACT: the window's vectors are exact tf32 values (bf16 / fp16 inputs used as
@@ -273,15 +276,15 @@ struct TcCursor {
 };
 
 
-__device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int64_t slot, int QT, int64_t Q,
-                                                   int64_t tokens, int64_t null_block, int64_t blocks) {
+__device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int64_t slot, int32_t kh, int QT,
+                                                   int64_t Q, int64_t tokens, int64_t null_block, int64_t blocks) {
   int mask = 0;
   for (int t = 0; t < QT; ++t) {
     const int64_t tok = bos + t;
     if (t < Q && t < eos - bos && tok >= 0 && tok < tokens) mask |= 1 << t;
   }
   const bool live = slot > null_block && slot < blocks;
-  return TcUnitMeta{mask ? static_cast<int32_t>(bos) : 0, live ? static_cast<int32_t>(slot) : -1, mask};
+  return TcUnitMeta{mask ? static_cast<int32_t>(bos) : 0, live ? static_cast<int32_t>(slot) : -1, mask | (kh << 8)};
 }
 
 // GATED: the fused gating prologue (raw a, b in the g / beta slots).
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     const int64_t bos = load_typed_index(p.qsl, static_cast<int64_t>(c.row) * p.qsl_stride, p.qsl_dtype);
     const int64_t eos = load_typed_index(p.qsl, static_cast<int64_t>(c.row + 1) * p.qsl_stride, p.qsl_dtype);
     const int64_t slot = load_typed_index(p.indices, static_cast<int64_t>(c.row) * p.index_stride, p.index_dtype);
-    return tc_unit_meta(bos, eos, slot, QT, p.query_len, p.tokens, p.null_block, p.blocks);
+    return tc_unit_meta(bos, eos, slot, c.hv / ratio, QT, p.query_len, p.tokens, p.null_block, p.blocks);
   };
   auto is_live = [&](const TcUnitMeta &m) { return m.slot >= 0; };
   // The unit two ahead: one thread starts asynchronous copies of its row's raw
@@ -346,13 +349,13 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     ptx::cp_async_small(&raw[2], idx + static_cast<int64_t>(c.row) * p.index_stride * ib, ib);
     ptx::cp_async_commit();
   };
-  auto decode_meta = [&](const uint64_t *raw) {
+  auto decode_meta = [&](const uint64_t *raw, const TcCursor &c) {  // thread kMetaThread
     auto val = [](uint64_t b, int32_t dt) {
       return dt == GDN_RSSM_I64 ? static_cast<int64_t>(b)
                                 : static_cast<int64_t>(static_cast<int32_t>(static_cast<uint32_t>(b)));
     };
-    return tc_unit_meta(val(raw[0], p.qsl_dtype), val(raw[1], p.qsl_dtype), val(raw[2], p.index_dtype), QT,
-                        p.query_len, p.tokens, p.null_block, p.blocks);
+    return tc_unit_meta(val(raw[0], p.qsl_dtype), val(raw[1], p.qsl_dtype), val(raw[2], p.index_dtype),
+                        c.hv / ratio, QT, p.query_len, p.tokens, p.null_block, p.blocks);
   };
   struct Inputs {  // one unit's activations in registers
     Act x[PER_WARP][EPL];  // q/k: vector warp + 8c, K elements 4 lane .. 4 lane + 3
@@ -366,9 +369,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   constexpr int GT = GATED ? 32 : 0;
   // Starts the loads of one unit's activations (nothing for null units).
   auto load_inputs = [&](Inputs &in, const TcCursor &c, const TcUnitMeta &m) {
-    const int vmask = is_live(m) ? m.vmask : 0;
+    const int vmask = is_live(m) ? m.vmask() : 0;
     const int hv = static_cast<int>(c.hv);
-    const int h = hv / ratio;
+    const int h = m.kh();
 #pragma unroll
     for (int cc = 0; cc < PER_WARP; ++cc) {
       const int j = warp + 8 * cc;
@@ -380,11 +383,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
 #pragma unroll
       for (int e = 0; e < EPL; ++e) in.x[cc][e] = live ? src[base + e] : from_f32<Act>(0.f);
     }
-    const Act *vin = static_cast<const Act *>(p.v);
+    const Act *vrow = static_cast<const Act *>(p.v) + static_cast<int64_t>(m.bos) * p.v_ts + hv * DIM + r;
 #pragma unroll
-    for (int t = 0; t < QT; ++t)
-      in.v[t] = ((vmask >> t) & 1) ? vin[(static_cast<int64_t>(m.bos) + t) * p.v_ts + hv * DIM + r]
-                                   : from_f32<Act>(0.f);
+    for (int t = 0; t < QT; ++t) in.v[t] = ((vmask >> t) & 1) ? vrow[t * p.v_ts] : from_f32<Act>(0.f);
     in.g = 0.f;
     in.beta = 0.f;
     const int gt = tid - GT;
@@ -467,8 +468,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     };
     const int64_t row = c0.row;
     const int hv = static_cast<int>(c0.hv);
-    const int h = hv / ratio;
-    const int vmask = m0.vmask;
+    const int h = m0.kh();
+    const int vmask = m0.vmask();
     const bool rec_ok = row < p.record_rows;
     Window &w = sm.win[i & 1];
 
@@ -484,7 +485,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
       if (tid == kMetaThread) {
         ptx::cp_async_wait_all();
-        sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1]);
+        sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1], c2);
       }
       __syncthreads();  // the previous unit's recurrence is done with its window buffer; metadata decoded
     } else {
@@ -531,7 +532,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         }
         if (j < QT) {
           // key record: packed -> every value head keeps its copy; typed -> once per key head
-          if (rec_ok && ((vmask >> t) & 1) && (packed || hv % ratio == 0)) {
+          if (rec_ok && ((vmask >> t) & 1) && (packed || h * ratio == hv)) {
             const int64_t kh = packed ? hv : h;
             const int32_t kd = packed ? GDN_RSSM_F32 : p.key_dtype;
 #pragma unroll
@@ -663,7 +664,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       }
       if (tid == kMetaThread) {  // the copies started a phase ago: decoded once, for everyone
         ptx::cp_async_wait_all();
-        sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1]);
+        sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1], c2);
       }
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
         if (tid == 0) atomicExch(p.status, kStatusMmaTimeout);
