@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   const int64_t units = p.rows * HV;
   const int64_t G = gridDim.x;
   const int ratio = static_cast<int>(HV / p.heads);
-  const bool normalize = (p.flags & GDN_RSSM_NORMALIZE_QK) != 0;
+  const bool normalize = !EXACT && (p.flags & GDN_RSSM_NORMALIZE_QK) != 0;  // exact operands: never
   const bool packed = (p.flags & GDN_RSSM_RECORD_PACKED) != 0;
   Act *out = static_cast<Act *>(p.out);
 
@@ -533,11 +533,16 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         if (j < QT) {
           // key record: packed -> every value head keeps its copy; typed -> once per key head
           if (rec_ok && ((vmask >> t) & 1) && (packed || h * ratio == hv)) {
-            const int64_t kh = packed ? hv : h;
-            const int32_t kd = packed ? GDN_RSSM_F32 : p.key_dtype;
+            const int64_t at = row * p.key_rs + (packed ? hv : h) * p.key_hs + t * p.key_ts + lane * EPL;
+            const int32_t kd = packed ? GDN_RSSM_F32 : p.key_dtype;  // one dtype switch per vector slice
+            if (kd == GDN_RSSM_F32) {
+              float *kp = static_cast<float *>(p.key) + at;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e)
-              store_key(p.key, row * p.key_rs + kh * p.key_hs + t * p.key_ts + lane * EPL + e, x[e], kd);
+              for (int e = 0; e < EPL; ++e) kp[e] = x[e];
+            } else {
+#pragma unroll
+              for (int e = 0; e < EPL; ++e) store_key(p.key, at + e, x[e], kd);
+            }
           }
         } else if constexpr (!EXACT) {  // exact operands keep q unscaled: the output is scaled instead
 #pragma unroll
