@@ -52,6 +52,21 @@
 
 namespace gdn_rssm {
 
+// (row, value head) of a CTA's units, advanced by gridDim.x units without a
+// 64-bit division per step.
+struct TcCursor {
+  int32_t row;
+  int32_t hv;
+  __device__ __forceinline__ void advance(int32_t dq, int32_t dr, int32_t HV) {
+    row += dq;
+    hv += dr;
+    if (hv >= HV) {
+      hv -= HV;
+      row += 1;
+    }
+  }
+};
+
 // A unit's row metadata, reduced to 32-bit fields when it is loaded (the host
 // keeps rows, tokens and blocks below 2^31): the token mask holds the window's
 // masking (t < Q, t < qlen, 0 <= bos + t < tokens), so bos only addresses valid
@@ -60,7 +75,8 @@ namespace gdn_rssm {
 // against the 80 that three resident CTAs leave per thread.
 struct TcUnitMeta {
   int32_t bos, slot;
-  int32_t vk;  // token mask (bits 0-7) | the key head the value head reads << 8
+  int32_t vk;       // token mask (bits 0-7) | the key head the value head reads << 8
+  int32_t row, hv;  // the unit
   __device__ __forceinline__ int vmask() const { return vk & 0xff; }
   __device__ __forceinline__ int kh() const { return vk >> 8; }
 };
@@ -108,6 +124,7 @@ struct VerifyTcShape {
     // the copy that step i + 1 starts before any barrier
     uint64_t meta_raw[2][3];
     TcUnitMeta meta[2];
+    TcCursor cur2;  // (row, value head) of the unit two ahead (Q <= 4): that thread's alone
     uint32_t tmem;
     float gpart[4][QT * QT];  // Gram partial sums per K slab
     Window win[2];
@@ -260,31 +277,19 @@ __device__ __forceinline__ void gram_finalize(const float (*part)[QT * QT], cons
   }
 }
 
-// (row, value head) of a CTA's units, advanced by gridDim.x units without a
-// 64-bit division per step.
-struct TcCursor {
-  int32_t row;
-  int32_t hv;
-  __device__ __forceinline__ void advance(int32_t dq, int32_t dr, int32_t HV) {
-    row += dq;
-    hv += dr;
-    if (hv >= HV) {
-      hv -= HV;
-      row += 1;
-    }
-  }
-};
 
 
-__device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int64_t slot, int32_t kh, int QT,
-                                                   int64_t Q, int64_t tokens, int64_t null_block, int64_t blocks) {
+__device__ __forceinline__ TcUnitMeta tc_unit_meta(int64_t bos, int64_t eos, int64_t slot, int32_t row, int32_t hv,
+                                                   int32_t kh, int QT, int64_t Q, int64_t tokens, int64_t null_block,
+                                                   int64_t blocks) {
   int mask = 0;
   for (int t = 0; t < QT; ++t) {
     const int64_t tok = bos + t;
     if (t < Q && t < eos - bos && tok >= 0 && tok < tokens) mask |= 1 << t;
   }
   const bool live = slot > null_block && slot < blocks;
-  return TcUnitMeta{mask ? static_cast<int32_t>(bos) : 0, live ? static_cast<int32_t>(slot) : -1, mask | (kh << 8)};
+  return TcUnitMeta{mask ? static_cast<int32_t>(bos) : 0, live ? static_cast<int32_t>(slot) : -1, mask | (kh << 8), row,
+                    hv};
 }
 
 // GATED: the fused gating prologue (raw a, b in the g / beta slots).
@@ -323,11 +328,12 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   Act *out = static_cast<Act *>(p.out);
 
   auto load_meta = [&](const TcCursor &c, bool in_range) {
-    if (!in_range) return TcUnitMeta{0, -1, 0};
+    if (!in_range) return TcUnitMeta{0, -1, 0, 0, 0};
     const int64_t bos = load_typed_index(p.qsl, static_cast<int64_t>(c.row) * p.qsl_stride, p.qsl_dtype);
     const int64_t eos = load_typed_index(p.qsl, static_cast<int64_t>(c.row + 1) * p.qsl_stride, p.qsl_dtype);
     const int64_t slot = load_typed_index(p.indices, static_cast<int64_t>(c.row) * p.index_stride, p.index_dtype);
-    return tc_unit_meta(bos, eos, slot, c.hv / ratio, QT, p.query_len, p.tokens, p.null_block, p.blocks);
+    return tc_unit_meta(bos, eos, slot, c.row, c.hv, c.hv / ratio, QT, p.query_len, p.tokens, p.null_block,
+                        p.blocks);
   };
   auto is_live = [&](const TcUnitMeta &m) { return m.slot >= 0; };
   // The unit two ahead: one thread starts asynchronous copies of its row's raw
@@ -354,7 +360,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       return dt == GDN_RSSM_I64 ? static_cast<int64_t>(b)
                                 : static_cast<int64_t>(static_cast<int32_t>(static_cast<uint32_t>(b)));
     };
-    return tc_unit_meta(val(raw[0], p.qsl_dtype), val(raw[1], p.qsl_dtype), val(raw[2], p.index_dtype),
+    return tc_unit_meta(val(raw[0], p.qsl_dtype), val(raw[1], p.qsl_dtype), val(raw[2], p.index_dtype), c.row, c.hv,
                         c.hv / ratio, QT, p.query_len, p.tokens, p.null_block, p.blocks);
   };
   struct Inputs {  // one unit's activations in registers
@@ -368,9 +374,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   // the gating prologue in the pass-1 window, where it has slack
   constexpr int GT = GATED ? 32 : 0;
   // Starts the loads of one unit's activations (nothing for null units).
-  auto load_inputs = [&](Inputs &in, const TcCursor &c, const TcUnitMeta &m) {
+  auto load_inputs = [&](Inputs &in, const TcUnitMeta &m) {
     const int vmask = is_live(m) ? m.vmask() : 0;
-    const int hv = static_cast<int>(c.hv);
+    const int hv = m.hv;
     const int h = m.kh();
 #pragma unroll
     for (int cc = 0; cc < PER_WARP; ++cc) {
@@ -398,31 +404,39 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       in.beta = p.dt_bias[hv];
     }
   };
-  auto issue_tile = [&](const TcCursor &c, const TcUnitMeta &m) {  // thread 0
+  auto issue_tile = [&](const TcUnitMeta &m) {  // thread 0
     if (p.flags & GDN_RSSM_VERIFY_TEST_NO_TILE) return;  // failure-detection test: the tile wait runs out
     ptx::mbar_arrive_expect_tx(&sm.tile_bar, Sh::TILE);
 #pragma unroll
     for (int mm = 0; mm < 4; ++mm)  // one 128-row box per 32-column K slab
-      ptx::tma_load_4d(tile + mm * Sh::SLAB, &state_map, &sm.tile_bar, mm * 32, 0, static_cast<int32_t>(c.hv),
-                       static_cast<int32_t>(m.slot));
+      ptx::tma_load_4d(tile + mm * Sh::SLAB, &state_map, &sm.tile_bar, mm * 32, 0, m.hv, m.slot);
   };
 
-  // ---- walk: cursors and metadata of units i, i + 1, i + 2 ------------------ //
+  // ---- walk: metadata of units i and i + 1 in registers; the cursor of unit
+  // i + 2 in shared memory, kept by the thread that copies and decodes its
+  // metadata ---------------------------------------------------------------- //
   const int32_t HV32 = static_cast<int32_t>(HV);
   const int32_t dq = static_cast<int32_t>(G / HV), dr = static_cast<int32_t>(G % HV);
-  TcCursor c0{static_cast<int32_t>(blockIdx.x / HV32), static_cast<int32_t>(blockIdx.x % HV32)};
-  TcCursor c1 = c0;
-  c1.advance(dq, dr, HV32);
-  TcCursor c2 = c1;
-  c2.advance(dq, dr, HV32);
-  TcUnitMeta m0 = load_meta(c0, true), m1 = load_meta(c1, blockIdx.x + G < units);
+  TcUnitMeta m0, m1;
+  // the cursor two ahead: in shared memory up to Q = 4, where every register
+  // counts against the 80 of three resident CTAs; in registers at Q = 8
+  TcCursor c2reg{0, 0};
+  TcCursor &c2 = QT >= 8 ? c2reg : sm.cur2;
+  {
+    TcCursor c{static_cast<int32_t>(blockIdx.x / HV32), static_cast<int32_t>(blockIdx.x % HV32)};
+    m0 = load_meta(c, true);
+    c.advance(dq, dr, HV32);
+    m1 = load_meta(c, blockIdx.x + G < units);
+    c.advance(dq, dr, HV32);
+    if (QT >= 8 || tid == kMetaThread) c2 = c;  // read after the first CTA barrier
+  }
 
   if (tid == 0) {
     ptx::prefetch_tensormap(&state_map);
     ptx::mbar_init(&sm.tile_bar, 1);
     ptx::mbar_init(&sm.mma_bar, 1);
     ptx::fence_mbar_init();
-    if (is_live(m0)) issue_tile(c0, m0);
+    if (is_live(m0)) issue_tile(m0);
   }
   if (warp == 0) {
     __syncwarp();  // the allocation is warp-wide (.sync.aligned)
@@ -450,7 +464,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   }
   const int gpair = Sh::GRAM_ALL ? gram_pair_rows<QT>(tid >> 2) : 0;  // this thread's Gram pair (Q = 8)
   Inputs ic;
-  load_inputs(ic, c0, m0);
+  load_inputs(ic, m0);
   ptx::tc_fence_before_sync();
   __syncthreads();
   ptx::tc_fence_after_sync();
@@ -464,10 +478,10 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     Inputs in;  // one unit ahead
     auto prefetch = [&]() {
       if (tid == kMetaThread) load_meta_async(sm.meta_raw[i & 1], c2, u + 2 * G < units);  // two units ahead
-      load_inputs(in, c1, m1);
+      load_inputs(in, m1);
     };
-    const int64_t row = c0.row;
-    const int hv = static_cast<int>(c0.hv);
+    const int64_t row = m0.row;
+    const int hv = m0.hv;
     const int h = m0.kh();
     const int vmask = m0.vmask();
     const bool rec_ok = row < p.record_rows;
@@ -482,7 +496,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
           out[(static_cast<int64_t>(m0.bos) + t) * p.out_ts + hv * DIM + (e % DIM)] = from_f32<Act>(0.f);
       }
       // the next unit's tile (this unit started none)
-      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
+      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(m1);
       if (tid == kMetaThread) {
         ptx::cp_async_wait_all();
         sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1], c2);
@@ -679,7 +693,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
       }
       mma_par ^= 1u;
       // ---- both passes done, the tile is free: start the next unit's load ---- //
-      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(c1, m1);
+      if (tid == 0 && u + G < units && is_live(m1)) issue_tile(m1);
       // ---- per-row recurrence: lane = state row of the warp's lane quadrant --- //
       ptx::tc_fence_after_sync();
       float d[NB], d2[16];
@@ -728,9 +742,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     ic = in;
     m0 = m1;
     m1 = sm.meta[i & 1];  // decoded before the last CTA barrier
-    c0 = c1;
-    c1 = c2;
-    c2.advance(dq, dr, HV32);
+    if (QT >= 8 || tid == kMetaThread) c2.advance(dq, dr, HV32);
   }
   // ---- release tensor memory (every path after the allocation) ---------------- //
   ptx::tc_fence_before_sync();
