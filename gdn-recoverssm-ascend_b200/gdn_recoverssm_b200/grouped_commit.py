@@ -175,14 +175,15 @@ class GroupedCommitBucket:
         self.max_blocks = max(int(c.num_blocks) for c in contexts)
         self._largest_pool = max(self.checkpoints, key=lambda t: t.shape[0])
         self.plan = torch.zeros(len(_PLAN_ROWS), capacity * len(contexts), dtype=torch.int32, device=self.device)
+        self._plan_rows = tuple(self.plan.unbind(0))  # row views made once (per-step host time)
 
-    source = property(lambda self: self.plan[0])
-    length = property(lambda self: self.plan[1])
-    final = property(lambda self: self.plan[2])
-    boundary = property(lambda self: self.plan[3])
-    boundary_len = property(lambda self: self.plan[4])
-    valid = property(lambda self: self.plan[5])
-    col = property(lambda self: self.plan[6])
+    source = property(lambda self: self._plan_rows[0])
+    length = property(lambda self: self._plan_rows[1])
+    final = property(lambda self: self._plan_rows[2])
+    boundary = property(lambda self: self._plan_rows[3])
+    boundary_len = property(lambda self: self._plan_rows[4])
+    valid = property(lambda self: self._plan_rows[5])
+    col = property(lambda self: self._plan_rows[6])
     state_addrs = property(lambda self: self.tables["state_addr"])
     state_block_strides = property(lambda self: self.tables["state_block"])
     conv_addrs = property(lambda self: self.tables["conv_addr"])
@@ -264,7 +265,7 @@ class GroupedCommitBucket:
                                                     persistent_accepted)
         ops = _native.ops()
         plan = _LaunchSpec("grouped_plan", ops.grouped_plan, (
-            sampled, *self._group_lists(payloads, self.contexts, align), *self.plan,
+            sampled, *self._group_lists(payloads, self.contexts, align), *self._plan_rows,
             idx_mapping, persistent_cols if align else None, persistent_accepted if align else None,
             rows, self.capacity, self.spec_query_len, align, bool(align and publish_align),
         ))

@@ -428,6 +428,7 @@ class GDNRecoverSSMCommitContext:
         self.record_bytes = sum(record_nbytes(r) for r in replays)
         self.tables = LayerTables(device, (self.checkpoints, self.conv_states, corrs, keys, decays))
         self.plan = torch.zeros(len(_PLAN_ROWS), max_num_reqs, dtype=torch.int32, device=device)
+        self._plan_rows = tuple(self.plan.unbind(0))  # row views made once (per-step host time)
         self.layer_groups = torch.zeros(len(self.checkpoints), dtype=torch.int32, device=device)
 
     # per-layer tables (row views of self.tables)
@@ -444,12 +445,12 @@ class GDNRecoverSSMCommitContext:
     decay_base_addrs = property(lambda self: self.tables["decay_addr"])
     decay_block_strides = property(lambda self: self.tables["decay_block"])
     # plan buffers (row views of self.plan)
-    commit_lens = property(lambda self: self.plan[0])
-    final_state_indices = property(lambda self: self.plan[1])
-    boundary_state_indices = property(lambda self: self.plan[2])
-    boundary_recovery_lens = property(lambda self: self.plan[3])
-    align_valid = property(lambda self: self.plan[4])
-    align_col = property(lambda self: self.plan[5])
+    commit_lens = property(lambda self: self._plan_rows[0])
+    final_state_indices = property(lambda self: self._plan_rows[1])
+    boundary_state_indices = property(lambda self: self._plan_rows[2])
+    boundary_recovery_lens = property(lambda self: self._plan_rows[3])
+    align_valid = property(lambda self: self._plan_rows[4])
+    align_col = property(lambda self: self._plan_rows[5])
 
     @classmethod
     def from_tensors(cls, conv_states, checkpoints, replays, *, spec_query_len: int, max_num_reqs: int,
@@ -506,11 +507,10 @@ class GDNRecoverSSMCommitContext:
         and the fold are programmatic dependents of the launch before each."""
         ops = _native.ops()
         batch = state_indices.shape[0]
-        plan_rows = (self.commit_lens, self.final_state_indices, self.boundary_state_indices,
-                     self.boundary_recovery_lens)
+        plan_rows = self._plan_rows[:4]
         specs = [_LaunchSpec("commit_plan", ops.commit_plan, (
-            accepted, request_indices, state_indices, qsl, block_table, computed, *self.plan, self.spec_query_len,
-            self.num_blocks, block_size))]
+            accepted, request_indices, state_indices, qsl, block_table, computed, *self._plan_rows,
+            self.spec_query_len, self.num_blocks, block_size))]
         if commit_conv:
             conv, t = self.conv_states[0], self.tables
             specs.append(_LaunchSpec("compact_conv", ops.compact_conv, (

@@ -61,6 +61,9 @@ class LayerTables:
         self.table = torch.tensor(values, dtype=torch.int64, device=device)
         self.owners = planes  # the addresses in the table stay valid while this object lives
         self.layers = layers
+        # the row views, made once: a commit passes several per step, and a
+        # view made per access costs host time on every step
+        self._rows = {name: self.table[i] for name, i in _INDEX.items()}
 
     def __getitem__(self, name: str) -> torch.Tensor:
-        return self.table[_INDEX[name]]
+        return self._rows[name]
