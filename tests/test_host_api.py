@@ -438,6 +438,20 @@ def test_algorithmic_byte_model_matches_the_survey_formula():
     fold = working * HV * D * D * 4 * 2 + 3 * HV * D * D * 4 + int(lens.sum()) * HV * (2 * D + 1) * 4 + 24 * B
     assert synthetic.commit_bytes(wl, lens, 3) == fold
     assert synthetic.conv_bytes(wl, lens, 3, 3) == (working + 3) * 8192 * 3 * 2 * 2
+    # the dim-first conv pool's sector floor: whole channel blocks of the
+    # source (read), the final page (read + write, or write when in place) and
+    # each boundary snapshot (read + write, or write when it is the source)
+    page = 8192 * 6 * 2
+    src = torch.arange(1, B + 1)
+    fin = torch.where(torch.arange(B) % 2 == 0, src, src + 1000)  # every other row in place
+    bnd = torch.zeros(B, dtype=torch.long)
+    written = torch.zeros(B, dtype=torch.bool)
+    bnd[2], written[2] = 2000, True     # a distinct boundary page (row 2 works, in place)
+    bnd[3], written[3] = src[3], True   # a boundary that is the source (row 3 works)
+    n_inplace = int(((lens > 0) & (fin == src)).sum())
+    n_moved = working - n_inplace
+    want_floor = (working + 2 * n_moved + n_inplace + 2 + 1) * page
+    assert synthetic.conv_floor_bytes(wl, lens, src, fin, bnd, written) == want_floor
     wl.a = act  # fused gating: raw a, b in the activation dtype instead of g, beta
     wl.b = act
     assert synthetic.verify_bytes(wl) == want - T * HV * 4
