@@ -190,6 +190,8 @@ static int verify_impl(const void *q, const void *k, const void *v, const void *
               "rows, tokens and checkpoint blocks must stay below 2^31");
   GDN_REQUIRE(p.blocks > 0 && p.record_rows >= 1, "state pool and record rows must be non-empty");
   GDN_REQUIRE(p.rows * p.value_heads < (int64_t(1) << 31), "rows x value heads exceeds the launch grid");
+  // the tensor-core walk packs a unit's key head above its 8-bit token mask
+  GDN_REQUIRE(p.value_heads < (int64_t(1) << 23), "value heads must stay below 2^23");
   if (p.rows == 0 || p.tokens == 0) return GDN_RSSM_OK;
   GDN_REQUIRE(q && k && v && g && beta && state && correction && key && decay && out && qsl && indices,
               "verify tensor pointer is null");
