@@ -337,8 +337,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   };
   auto is_live = [&](const TcUnitMeta &m) { return m.slot >= 0; };
   // The unit two ahead: one thread starts asynchronous copies of its row's raw
-  // qsl / slot entries into shared memory (no registers held, no stall);
-  // everyone decodes them after the next CTA barrier.
+  // qsl / slot entries into shared memory (no registers held, no stall) and
+  // decodes them, once they have landed, for everyone to read after the next
+  // CTA barrier.
   constexpr int kMetaThread = 64;
   auto load_meta_async = [&](uint64_t *raw, const TcCursor &c, bool in_range) {  // thread kMetaThread
     if (!in_range) {
