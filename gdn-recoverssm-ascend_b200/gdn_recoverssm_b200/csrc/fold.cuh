@@ -10,16 +10,19 @@
 //     store h to the final page.
 // The update is the reference's exact arithmetic order (tl.fma(c, k, h*d)).
 //
-// B200 design: one CTA (256 threads) per unit, three resident per SM.  Thread
-// 0 starts one bulk copy (cp.async.bulk, completion on an mbarrier) of the
-// source state tile into shared memory -- 64 KiB in flight per CTA without
-// holding registers -- while all threads stage the window's corr / decay
-// records in shared memory and their key slice in registers (each thread
-// owns one 16-byte column chunk of the tile and a strided set of rows).  The
-// fold then streams the final state, and the boundary snapshot mid-fold,
-// straight to HBM with 16-byte stores.  The whole source tile is in shared
-// memory before any store of the unit, so in-place commits and a boundary
-// page that aliases the source page are safe.
+// B200 design: one CTA (256 threads) per unit, three resident per SM -- or,
+// for fp32 tiles at K = V = 128, two CTAs of 128 threads per unit, each
+// folding 64 of the 128 state rows, six resident per SM (PARTS below).
+// Thread 0 starts one bulk copy (cp.async.bulk, completion on an mbarrier) of
+// the CTA's rows of the source state tile into shared memory -- 64 (or 32)
+// KiB in flight per CTA without holding registers -- while all threads stage
+// the window's corr / decay records in shared memory and their key slice in
+// registers (each thread owns one 16-byte column chunk of the tile and a
+// strided set of rows).  The fold then streams the final state, and the
+// boundary snapshot mid-fold, straight to HBM with 16-byte stores.  The
+// CTA's whole source rows are in shared memory before any of its stores, and
+// no two CTAs share a row, so in-place commits and a boundary page that
+// aliases the source page are safe.
 #pragma once
 
 #include "params.cuh"

@@ -34,13 +34,17 @@
 //             decay / beta from the raw inputs here;
 //   thread 0: pass 2 right behind pass 1, one commit for both;
 //   warps 4+: Gram coefficients (warp 0, which issues the MMAs, takes no
-//             part in the Gram); after the commit, thread 0 starts the NEXT
+//             part in the Gram); the metadata thread decodes its copy (token
+//             mask, slot, key head) for everyone to read after the barrier;
+//             after the commit, thread 0 starts the NEXT
 //             unit's tile (4-D tensor map, 128-byte swizzle -- the layout
 //             the MMA's K-major descriptor reads directly -- one 128-row box
 //             per K slab) into the freed buffer, and every warp loads its 32
 //             rows' sums from tensor memory (one row per lane) and runs the
-//             recurrence -- warps 0-3 write the correction records, warps
-//             4-7 the outputs -- while that load is in flight.
+//             recurrence (all window tokens, no mask test: a masked token's
+//             correction is a signed zero) -- warps 0-3 write the correction
+//             records, warps 4-7 the outputs, stores masked -- while that
+//             load is in flight.
 // Three CTA barriers per unit; the per-unit scalars are double-buffered by
 // unit parity.  Every wait is bounded (1 s) and reported through the status
 // word; tensor memory is released on every path after it was allocated.
