@@ -64,8 +64,14 @@ __device__ __forceinline__ RowPlan context_row_plan(const CommitPlanParams &p, i
   int32_t blen = 0, colv = 0, c = 0;
   const bool align = p.table.data != nullptr;
   if (align) {
-    c = static_cast<int32_t>(load_index_checked(p.computed, req, row_ok));
-    if (req < 0 || req >= p.table.rows) row_ok = false;
+    // a request without a computed count or a block-table row makes the row
+    // invalid and its align arithmetic start from zero (the stored column too)
+    bool have = true;
+    c = static_cast<int32_t>(load_index_checked(p.computed, req, have));
+    if (!have || req < 0 || req >= p.table.rows) {
+      row_ok = false;
+      c = 0;
+    }
     const int32_t W = static_cast<int32_t>(p.table.cols), B = static_cast<int32_t>(p.block_size);  // B >= 1
     const int32_t end = add_wrap32(c, n);
     const int32_t last = add_wrap32(end, -1);
@@ -136,8 +142,12 @@ __device__ __forceinline__ RowPlan group_row_plan(const GroupedPlanParams &p, in
   int64_t fin = source, boundary = nul, blen = 0, colv = 0;
   bool computed_ok = true;
   if (p.align) {
-    const int64_t c = load_index_checked(g.num_computed, req, row_ok);
-    if (req < 0 || req >= g.block_table.rows) row_ok = false;
+    bool have = true;  // as in context_row_plan: no computed count or table row -> invalid, from zero
+    int64_t c = load_index_checked(g.num_computed, req, have);
+    if (!have || req < 0 || req >= g.block_table.rows) {
+      row_ok = false;
+      c = 0;
+    }
     computed_ok = c >= 0;
     const int64_t B = g.block_size, W = g.block_table.cols;
     const int64_t pos = c + n;
