@@ -35,6 +35,11 @@ CASES = [
     (7, torch.float16, "packed", True, 2, 4, torch.float32),
     (6, torch.bfloat16, "soa", True, 1, 4, torch.float32),
     (4, torch.bfloat16, "packed", False, 2, 4, torch.bfloat16),
+    # exact operands with a window shorter than the instantiation's (Q = 3 on
+    # the 4-token kernel, Q = 6 on the 8-token one): the tokens past Q are
+    # masked through the mask-free correction chain
+    (3, torch.bfloat16, "packed", False, 2, 4, torch.float32),
+    (6, torch.bfloat16, "packed", False, 1, 4, torch.float32),
 ]
 
 
