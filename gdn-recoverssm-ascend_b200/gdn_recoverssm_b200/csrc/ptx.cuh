@@ -32,6 +32,12 @@ __device__ __forceinline__ void cp_async_small(void *smem_dst, const void *gsrc,
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
 }
+// As cp_async16, but copies nothing and zero-fills the 16 bytes when !full.
+__device__ __forceinline__ void cp_async16_zfill(void *smem_dst, const void *gsrc, bool full) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem_dst)), "l"(gsrc),
+               "r"(full ? 16 : 0)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 

@@ -52,7 +52,16 @@ int launch_verify_kernel(VerifyLaunch &L) {
   // operands: bf16 / fp16 q, k used as given are exact tf32 values
   const int gated = (L.p.flags & kGateInKernel) ? 1 : 0;
   constexpr bool low_precision = !std::is_same<Act, float>::value;
-  const int exact = (TC && low_precision && !(L.p.flags & GDN_RSSM_NORMALIZE_QK)) ? 1 : 0;
+  // at Q = 8 the exact form stages q / k / v rows with 16-byte cp.async: it
+  // needs 16-byte aligned rows (else the split form runs, same results)
+  auto rows16 = [&]() {
+    const int64_t es = static_cast<int64_t>(sizeof(Act));
+    return ((reinterpret_cast<uintptr_t>(L.p.q) | reinterpret_cast<uintptr_t>(L.p.k) |
+             reinterpret_cast<uintptr_t>(L.p.v)) & 15) == 0 &&
+           (L.p.q_ts * es) % 16 == 0 && (L.p.k_ts * es) % 16 == 0 && (L.p.v_ts * es) % 16 == 0;
+  };
+  const int exact =
+      (TC && low_precision && !(L.p.flags & GDN_RSSM_NORMALIZE_QK) && (QT < 8 || rows16())) ? 1 : 0;
   void (*kernel)(const CUtensorMap, const VerifyParams) = nullptr;
   int smem = 0;
   if constexpr (TC) {

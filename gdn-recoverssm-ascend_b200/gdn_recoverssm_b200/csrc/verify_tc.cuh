@@ -111,6 +111,14 @@ struct VerifyTcShape {
   // j * 512 bytes, for the Gram on every warp (gram_all_warps)
   static constexpr bool GRAM_ALL = QT >= 8;
   static constexpr int X32_BYTES = GRAM_ALL ? NJ * DIM * 4 : 0;
+  // Q = 8 with exact (2-byte) operands: the next unit's q / k / v rows come
+  // into shared memory by cp.async (two buffers, by unit parity) instead of
+  // registers -- the 8-token walk is at the 128 registers two CTAs leave.
+  // The host selects this form only for 16-byte aligned activation rows.
+  static constexpr bool SIN = EXACT && QT >= 8;
+  static constexpr int IN_X = NJ * DIM * static_cast<int>(sizeof(Act));  // one unit's [k; q] rows
+  static constexpr int IN_V = QT * DIM * static_cast<int>(sizeof(Act));  // one unit's v rows
+  static constexpr int IN_BYTES = SIN ? 2 * (IN_X + IN_V) : 0;
   struct Window {  // per-unit scalars
     float A[QT];
     float beta[QT];
@@ -136,7 +144,7 @@ struct VerifyTcShape {
   // tile | pass-2 operand | pass-1 operand | fp32 X (Q = 8) | scalars; the
   // dynamic shared memory base is 1024-byte aligned (checked at run time), as
   // the 128-byte swizzle atoms require
-  static constexpr int SMEM = TILE + B2_BYTES + B_BYTES + X32_BYTES + static_cast<int>(sizeof(Small));
+  static constexpr int SMEM = TILE + B2_BYTES + B_BYTES + X32_BYTES + IN_BYTES + static_cast<int>(sizeof(Small));
   static_assert(NB <= static_cast<int>(D2_COL) && (NB == 16 || NB == 32), "accumulator columns");
   static_assert(!EXACT || !std::is_same<Act, float>::value, "fp32 activations are not exact tf32 values");
   static_assert(NJ <= NB2, "pass-2 operand rows");
@@ -317,7 +325,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   unsigned char *b2op = smem_raw + Sh::TILE;  // pass-2 operand: bf16(X)
   unsigned char *bop = b2op + Sh::B2_BYTES;    // pass-1 operand: [hi(X); lo(X)]
   float *x32 = reinterpret_cast<float *>(bop + Sh::B_BYTES);  // fp32 X (Q = 8)
-  Small &sm = *reinterpret_cast<Small *>(bop + Sh::B_BYTES + Sh::X32_BYTES);
+  unsigned char *in_buf = bop + Sh::B_BYTES + Sh::X32_BYTES;  // staged activations (SIN), 2 buffers
+  Small &sm = *reinterpret_cast<Small *>(in_buf + Sh::IN_BYTES);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -378,11 +387,32 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   // plain: warp 0 turns g into the decay while staging; gated: warp 1 runs
   // the gating prologue in the pass-1 window, where it has slack
   constexpr int GT = GATED ? 32 : 0;
-  // Starts the loads of one unit's activations (nothing for null units).
-  auto load_inputs = [&](Inputs &in, const TcUnitMeta &m) {
+  // Starts the loads of one unit's activations (nothing for null units); with
+  // SIN the q / k / v rows go to shared-memory buffer `b` by cp.async (masked
+  // tokens zero-filled) and only g / beta to registers.
+  auto load_inputs = [&](Inputs &in, const TcUnitMeta &m, int b) {
     const int vmask = is_live(m) ? m.vmask() : 0;
     const int hv = m.hv;
     const int h = m.kh();
+    if constexpr (Sh::SIN) {
+      constexpr int CPV = DIM * static_cast<int>(sizeof(Act)) / 16;  // 16-byte chunks per row
+      unsigned char *xb = in_buf + b * (Sh::IN_X + Sh::IN_V);
+      {
+        const int j = tid / CPV, c = tid % CPV;  // NJ x CPV == 256 chunks: one per thread
+        const int t = j % QT;
+        const bool live = (vmask >> t) & 1;
+        const Act *src = static_cast<const Act *>(j >= QT ? p.q : p.k) +
+                         (static_cast<int64_t>(m.bos) + t) * (j >= QT ? p.q_ts : p.k_ts) + h * DIM + c * 8;
+        ptx::cp_async16_zfill(xb + j * DIM * sizeof(Act) + c * 16, live ? src : p.q, live);
+      }
+      if (tid < QT * CPV) {
+        const int t = tid / CPV, c = tid % CPV;
+        const bool live = (vmask >> t) & 1;
+        const Act *src = static_cast<const Act *>(p.v) + (static_cast<int64_t>(m.bos) + t) * p.v_ts + hv * DIM + c * 8;
+        ptx::cp_async16_zfill(xb + Sh::IN_X + t * DIM * sizeof(Act) + c * 16, live ? src : p.v, live);
+      }
+      ptx::cp_async_commit();
+    } else {
 #pragma unroll
     for (int cc = 0; cc < PER_WARP; ++cc) {
       const int j = warp + 8 * cc;
@@ -397,6 +427,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     const Act *vrow = static_cast<const Act *>(p.v) + static_cast<int64_t>(m.bos) * p.v_ts + hv * DIM + r;
 #pragma unroll
     for (int t = 0; t < QT; ++t) in.v[t] = ((vmask >> t) & 1) ? vrow[t * p.v_ts] : from_f32<Act>(0.f);
+    }
     in.g = 0.f;
     in.beta = 0.f;
     const int gt = tid - GT;
@@ -469,7 +500,8 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
   }
   const int gpair = Sh::GRAM_ALL ? gram_pair_rows<QT>(tid >> 2) : 0;  // this thread's Gram pair (Q = 8)
   Inputs ic;
-  load_inputs(ic, m0);
+  load_inputs(ic, m0, 0);
+  if constexpr (Sh::SIN) ptx::cp_async_wait_all();  // unit 0's rows staged before the barrier
   ptx::tc_fence_before_sync();
   __syncthreads();
   ptx::tc_fence_after_sync();
@@ -483,7 +515,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
     Inputs in;  // one unit ahead
     auto prefetch = [&]() {
       if (tid == kMetaThread) load_meta_async(sm.meta_raw[i & 1], c2, u + 2 * G < units);  // two units ahead
-      load_inputs(in, m1);
+      load_inputs(in, m1, static_cast<int>((i + 1) & 1));
     };
     const int64_t row = m0.row;
     const int hv = m0.hv;
@@ -494,6 +526,9 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
 
     if (!is_live(m0)) {
       // ---- null / out-of-pool slot: zero output, nothing loaded ------------ //
+      // staged rows: the previous unit's recurrence may still read the v rows
+      // of the buffer this prefetch refills -- a CTA barrier first
+      if constexpr (Sh::SIN) __syncthreads();
       prefetch();
       for (int e = tid; e < QT * DIM; e += kVerifyThreads) {
         const int t = e / DIM;
@@ -506,6 +541,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         ptx::cp_async_wait_all();
         sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1], c2);
       }
+      if constexpr (Sh::SIN) ptx::cp_async_wait_all();  // the next unit's rows staged
       __syncthreads();  // the previous unit's recurrence is done with its window buffer; metadata decoded
     } else {
       // ---- stage the window --------------------------------------------------- //
@@ -537,8 +573,16 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         if (j >= NJ) continue;
         const int t = j % QT;
         float *x = xs[c];
+        if constexpr (Sh::SIN) {  // this vector's 4 elements of the staged rows: one 8-byte read
+          const uint2 raw = *reinterpret_cast<const uint2 *>(in_buf + (i & 1) * (Sh::IN_X + Sh::IN_V) +
+                                                             (j * DIM + lane * EPL) * sizeof(Act));
+          const Act *e4 = reinterpret_cast<const Act *>(&raw);
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) x[e] = to_f32<Act>(ic.x[c][e]);
+          for (int e = 0; e < EPL; ++e) x[e] = to_f32<Act>(e4[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) x[e] = to_f32<Act>(ic.x[c][e]);
+        }
         if (normalize) {
           float ss = 0.f;
 #pragma unroll
@@ -690,6 +734,7 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         ptx::cp_async_wait_all();
         sm.meta[i & 1] = decode_meta(sm.meta_raw[i & 1], c2);
       }
+      if constexpr (Sh::SIN) ptx::cp_async_wait_all();  // the next unit's rows, staged a phase ago
       if (__syncthreads_or(!ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs))) {
         if (tid == 0) atomicExch(p.status, kStatusMmaTimeout);
         ptx::mbar_wait_bounded(&sm.mma_bar, mma_par, kWaitLimitNs);
@@ -722,7 +767,12 @@ __global__ void __launch_bounds__(kVerifyThreads, verify_tc_min_blocks<QT>())
         float kv = w.A[t] * (EXACT ? d[t] : (d[t] + d[NJ + t]) + d2[t]);
 #pragma unroll
         for (int s2 = 0; s2 < t; ++s2) kv = fmaf(w.mkk[t][s2], cr[s2], kv);
-        cr[t] = w.beta[t] * (to_f32<Act>(ic.v[t]) - kv);
+        float vt;
+        if constexpr (Sh::SIN)
+          vt = to_f32<Act>(reinterpret_cast<const Act *>(in_buf + (i & 1) * (Sh::IN_X + Sh::IN_V) + Sh::IN_X)[t * DIM + r]);
+        else
+          vt = to_f32<Act>(ic.v[t]);
+        cr[t] = w.beta[t] * (vt - kv);
       }
       if (warp < 4) {  // correction records
         if (rec_ok) {

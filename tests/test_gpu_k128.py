@@ -157,16 +157,18 @@ def test_verify_k128_matches_oracle(pkg, case):
                 assert_fp32_close(g_np[m], want[m], what=name)
 
 
-def test_verify_k128_long_walks_alternating_live_and_null_rows(pkg):
+@pytest.mark.parametrize("Q", [4, 8])
+def test_verify_k128_long_walks_alternating_live_and_null_rows(pkg, Q):
     """Many units per CTA (2048 rows x 8 value heads over the persistent
-    grid, ~37 units per CTA) with live, null, negative and out-of-pool slots
-    and empty windows interleaved at random, so that every CTA's walk switches
-    between its live and null paths many times: every unit's outputs and
-    records against the float64 restatement, null rows' outputs zero and their
-    records untouched."""
+    grid, ~37 units per CTA at Q = 4, ~55 at Q = 8) with live, null, negative
+    and out-of-pool slots and empty windows interleaved at random, so that
+    every CTA's walk switches between its live and null paths many times (at
+    Q = 8 the next unit's rows are staged in shared memory, refilled across
+    those switches): every unit's outputs and records against the float64
+    restatement, null rows' outputs zero and their records untouched."""
     from tests.torch_reference import rel_errors_per_unit, rounded_ok, verify_rows
 
-    B, H, HV, Q, blocks = 2048, 2, 8, 4, 64
+    B, H, HV, blocks = 2048, 2, 8, 64
     gen = torch.Generator().manual_seed(77)
     kind = torch.randint(0, 10, (B,), generator=gen)
     slots = 1 + torch.randint(0, blocks - 1, (B,), generator=gen)
