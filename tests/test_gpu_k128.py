@@ -40,6 +40,8 @@ CASES = [
     # masked through the mask-free correction chain
     (3, torch.bfloat16, "packed", False, 2, 4, torch.float32),
     (6, torch.bfloat16, "packed", False, 1, 4, torch.float32),
+    # fp16 exact operands at Q = 8: activations staged in shared memory
+    (8, torch.float16, "packed", False, 2, 4, torch.float32),
 ]
 
 
