@@ -24,7 +24,8 @@
 // units blockIdx.x, blockIdx.x + gridDim.x, ...; per unit:
 //   all:      stage [hi(X); lo(X)], decay / beta and the decay and key
 //             records (the unit's q/k/v/g/beta were loaded into registers
-//             during the previous unit); wait for the tile;
+//             during the previous unit -- at Q = 8 with exact operands its
+//             q/k/v rows into shared memory by cp.async); wait for the tile;
 //   thread 0: pass 1, no commit yet;
 //   all:      meanwhile bf16(lo(S)) -> tensor memory (one row per lane),
 //             bf16(X) -> the pass-2 operand; warps 4-7 the Gram partial
