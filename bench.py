@@ -358,19 +358,50 @@ def run_b200(args):
         align_kw = dict(block_table=wl.block_table, num_computed_tokens=wl.num_computed,
                         mamba_block_size=wl.block_size)
 
-    def verify():
-        if args.gated:
-            g.gdn_recoverssm_verify_gated(wl.A_log, wl.a, wl.b, wl.dt_bias, wl.q, wl.k, wl.v,
-                                          checkpoint_state=wl.state, replay_cache=wl.records, query_start_loc=wl.qsl,
-                                          state_indices=wl.state_indices, spec_query_len=wl.Q,
-                                          use_qk_l2norm_in_kernel=False, out=wl.out)
-        else:
-            g.gdn_recoverssm_verify(wl.g, wl.beta, wl.q, wl.k, wl.v, checkpoint_state=wl.state,
-                                    replay_cache=wl.records, query_start_loc=wl.qsl, state_indices=wl.state_indices,
-                                    spec_query_len=wl.Q, out=wl.out)
+    # --grouped-layers L: L GDN layers (each its own state pool, conv pool and
+    # records; the same inputs and metadata), L verifies and ONE grouped commit
+    # of the L groups in one bucket -- the serving commit of a KV-cache group
+    # set (grouped plan, conv compaction and fold over every layer at once)
+    layers = [(wl, ctx)]
+    for _ in range(1, args.grouped_layers):
+        w2 = synthetic.make(args.config, dev, seed=0, world=shard_world, rank=shard_rank,
+                            conv_dim=args.conv_dim if conv else 16, rows=args.rows, pool=args.pool, gated=args.gated)
+        layers.append((w2, g.GDNRecoverSSMCommitContext.from_tensors([w2.conv], [w2.state], [w2.records],
+                                                                      spec_query_len=w2.Q, max_num_reqs=w2.B)))
 
-    specs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=conv, **align_kw)
-    names = [sp.name for sp in specs]  # commit_plan, (compact_conv,) fold
+    def verify():
+        for lw, _ in layers:
+            if args.gated:
+                g.gdn_recoverssm_verify_gated(lw.A_log, lw.a, lw.b, lw.dt_bias, lw.q, lw.k, lw.v,
+                                              checkpoint_state=lw.state, replay_cache=lw.records,
+                                              query_start_loc=lw.qsl, state_indices=lw.state_indices,
+                                              spec_query_len=lw.Q, use_qk_l2norm_in_kernel=False, out=lw.out)
+            else:
+                g.gdn_recoverssm_verify(lw.g, lw.beta, lw.q, lw.k, lw.v, checkpoint_state=lw.state,
+                                        replay_cache=lw.records, query_start_loc=lw.qsl,
+                                        state_indices=lw.state_indices, spec_query_len=lw.Q, out=lw.out)
+
+    if args.grouped_layers:
+        from types import SimpleNamespace
+
+        rows_host = tuple(range(wl.B))
+        qlens = tuple(int(x) for x in (wl.qsl[1:] - wl.qsl[:-1]).cpu())
+        entries = []
+        for lw, lctx in layers:
+            payload = SimpleNamespace(
+                state_indices=lw.state_indices, query_start_loc=lw.qsl,
+                request_indices=torch.arange(wl.B, dtype=torch.int32, device=dev),
+                block_table=lw.block_table, num_computed_tokens=lw.num_computed, block_size=lw.block_size,
+                request_rows=rows_host, query_lens=qlens)
+            entries.append(g.CommitEntry(SimpleNamespace(recoverssm_commit=payload), payload, lctx))
+        bucket = g.GroupedCommitBucket(tuple(lctx for _, lctx in layers))
+        persistent = [torch.zeros(wl.B, dtype=torch.int32, device=dev) for _ in range(2)]
+        specs = bucket.make_specs(entries, wl.accepted, torch.arange(wl.B, dtype=torch.int32, device=dev),
+                                  *persistent, publish_align=True)
+        conv = True  # the grouped commit always compacts the conv history
+    else:
+        specs = ctx.make_commit_specs(wl.accepted, wl.state_indices, wl.qsl, commit_conv=conv, **align_kw)
+    names = [sp.name for sp in specs]  # (grouped_)plan, (compact_conv,) fold
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -398,9 +429,14 @@ def run_b200(args):
         graph.replay()
         barrier()
     # plan outputs are identical every step (same metadata): byte model inputs
-    lens = ctx.commit_lens[: wl.B].cpu()
-    bnd = ((ctx.boundary_state_indices[: wl.B] > 0) & (ctx.boundary_recovery_lens[: wl.B] > 0)
-           & (ctx.boundary_state_indices[: wl.B] != ctx.final_state_indices[: wl.B])).cpu()
+    if args.grouped_layers:  # group 0's rows of the bucket's plan
+        plan_len, plan_final = bucket.length[: wl.B], bucket.final[: wl.B]
+        plan_boundary, plan_blen = bucket.boundary[: wl.B], bucket.boundary_len[: wl.B]
+    else:
+        plan_len, plan_final = ctx.commit_lens[: wl.B], ctx.final_state_indices[: wl.B]
+        plan_boundary, plan_blen = ctx.boundary_state_indices[: wl.B], ctx.boundary_recovery_lens[: wl.B]
+    lens = plan_len.cpu()
+    bnd = ((plan_boundary > 0) & (plan_blen > 0) & (plan_boundary != plan_final)).cpu()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2 + len(specs))] for _ in range(args.steps)]
     with ClockSampler(dev) as clocks:
         barrier()
@@ -447,11 +483,12 @@ def run_b200(args):
     if rank != 0:
         return 0
     peak, peak_kind = _peaks()
-    vbytes = synthetic.verify_bytes(wl)
-    fbytes = synthetic.commit_bytes(wl, lens, int(bnd.sum()))
-    cbytes = synthetic.conv_bytes(wl, lens, int(bnd.sum()), ctx.conv_history_len) if conv else 0
-    cfloor = synthetic.conv_floor_bytes(wl, lens, wl.state_indices[: wl.B].cpu(), ctx.final_state_indices[: wl.B].cpu(),
-                                        ctx.boundary_state_indices[: wl.B].cpu(), bnd) if conv else 0
+    L = len(layers)  # every layer moves the same bytes (same inputs and metadata)
+    vbytes = L * synthetic.verify_bytes(wl)
+    fbytes = L * synthetic.commit_bytes(wl, lens, int(bnd.sum()))
+    cbytes = L * synthetic.conv_bytes(wl, lens, int(bnd.sum()), ctx.conv_history_len) if conv else 0
+    cfloor = L * synthetic.conv_floor_bytes(wl, lens, wl.state_indices[: wl.B].cpu(),
+                                            plan_final[: wl.B].cpu(), plan_boundary[: wl.B].cpu(), bnd) if conv else 0
     verify_gbs = vbytes / (verify_ms * 1e-3) / 1e9
     step_gbs = (vbytes + fbytes + cbytes) / (step_ms * 1e-3) / 1e9
     kernels = {"verify": {"ms": verify_ms, "bytes": vbytes, "GB/s": verify_gbs, "frac": verify_gbs / peak}}
@@ -482,18 +519,22 @@ def run_b200(args):
                      "achieved": kernels[top]["GB/s"], "peak": peak, "unit": "GB/s", "frac": kernels[top]["frac"],
                      "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": bytes_of[top]},
         "kernels": kernels,
-        "gpu_launches": (1 + len(specs)) * args.steps * world,  # verify + the commit launches, per step and rank
+        "gpu_launches": (L + len(specs)) * args.steps * world,  # the verifies + the commit launches, per step and rank
         "clocks": clk,
         "device_status": status,
     }
     line["config"]["commit_launches"] = names
+    if args.grouped_layers:
+        line["config"]["grouped_commit"] = (f"{L} GDN layers: {L} verifies and one grouped commit of one bucket "
+                                            f"of {L} groups per step (bytes counted for every layer); e2e is the "
+                                            f"single-layer public-API step")
     line["config"]["launch"] = (f"CUDA graph of {gsteps} steps, replayed" if graphed
                                 else "eager: each step issued from Python")
     line["host_issue_ms_per_step"] = host_issue_ms
     if args.shard_of:
         line["config"]["parallelism"] = f"rank 0 of a {args.shard_of}-way v-head split, on one GPU (profiling only)"
     if conv:
-        line["config"]["commit_conv"] = f"conv history compacted in the commit: {args.conv_dim} channels"
+        line["config"]["commit_conv"] = f"conv history compacted in the commit: {int(wl.conv.shape[1])} channels"
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(args.config, rows_sample=args.cpu_rows, gated=args.gated)
         line["cpu_baseline"]["nproc"] = os.cpu_count()
@@ -607,6 +648,8 @@ def main(argv=None):
                     help="verify through the fused-gating entry point (raw a, b, A_log, dt_bias)")
     ap.add_argument("--e2e-buffers", type=int, default=3, help="device input/output buffers of the end-to-end loop")
     ap.add_argument("--e2e-steps", type=int, default=50, help="fewest steps the end-to-end pass times")
+    ap.add_argument("--grouped-layers", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="L GDN layers committed by one grouped-commit bucket per step (0: the per-context commit)")
     ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
                     help="headline steps replayed from a CUDA graph, or issued one by one from Python")
     ap.add_argument("--rows", type=int, default=None, help="reduced batch (profiling cases only)")
