@@ -346,6 +346,31 @@ def test_context_tables_and_validation():
                    torch.tensor([0, 4, 8], dtype=torch.int32), block_table=torch.zeros(2, 4, dtype=torch.int32))
 
 
+def test_context_views_are_made_once_and_share_storage():
+    """The plan and table row views a commit passes every step are made once
+    at construction: the same tensor objects on every access and every step's
+    specs, views of the one plan / table tensor (so a launch's writes show in
+    them)."""
+    import gdn_recoverssm_b200 as g
+
+    ctx = _context(g)
+    rows = (ctx.commit_lens, ctx.final_state_indices, ctx.boundary_state_indices, ctx.boundary_recovery_lens,
+            ctx.align_valid, ctx.align_col)
+    assert all(a is b for a, b in zip(rows, (ctx.commit_lens, ctx.final_state_indices, ctx.boundary_state_indices,
+                                             ctx.boundary_recovery_lens, ctx.align_valid, ctx.align_col)))
+    for i, r in enumerate(rows):
+        assert r.data_ptr() == ctx.plan[i].data_ptr() and r.shape == ctx.plan[i].shape
+    ctx.plan[1].fill_(5)
+    assert int(ctx.final_state_indices.sum()) == 5 * ctx.plan.shape[1]
+    assert ctx.state_base_addrs is ctx.state_base_addrs and ctx.key_block_strides is ctx.key_block_strides
+    assert ctx.state_base_addrs.data_ptr() == ctx.tables.table[0].data_ptr()
+    args = (torch.ones(2, dtype=torch.int32), torch.tensor([1, 2], dtype=torch.int32),
+            torch.tensor([0, 4, 8], dtype=torch.int32))
+    a, b = ctx.make_commit_specs(*args), ctx.make_commit_specs(*args)
+    assert all(x is y for x, y in zip(a[-1].args, b[-1].args) if isinstance(x, torch.Tensor) and x.dim() == 1
+               and x.dtype == torch.int64), "the fold's table views are the same objects every step"
+
+
 def _entry(g, context, group=0, align=True):
     from types import SimpleNamespace
 
