@@ -245,8 +245,9 @@ def _verify(g, beta, q, k, v, checkpoint_state, replay_cache, query_start_loc, s
     HV, V = vshape[2], vshape[3]
     _require(H > 0 and HV >= H and HV % H == 0, "value heads must be a positive multiple of the q/k heads")
     _require(g.numel() == total * HV and beta.numel() == total * HV, "gate or beta shape is incompatible")
-    g2 = g.reshape(total, HV)
-    beta2 = beta.reshape(total, HV)
+    # [T, HV] as given, else a view (a reshape per call costs host time per step)
+    g2 = g if g.shape == (total, HV) else g.reshape(total, HV)
+    beta2 = beta if beta.shape == (total, HV) else beta.reshape(total, HV)
     gs, bs = g2.stride(), beta2.stride()
     _require(gs[1] == 1 and bs[1] == 1, "gate and beta heads must be contiguous")
     _require(0 < spec_query_len <= MAX_SPEC_QUERY_LEN, f"spec_query_len must be in [1, {MAX_SPEC_QUERY_LEN}]")
